@@ -1,0 +1,129 @@
+// internal.hpp -- handle layout and helpers shared by the host translation units.
+#pragma once
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <vector>
+
+#include "crt.hpp"
+#include "ggemm.h"
+#include "ggemm_stages.h"
+#include "kernels.cuh"
+#include "planner.hpp"
+#include "reuse.hpp"
+
+namespace g2 {
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+inline size_t c_plane_elems(int m, int n) { return align_up((size_t)m * (size_t)n, 64); }
+inline size_t ws_ints(int rows) { return align_up(4 * (size_t)rows, 64); }
+// Bytes of all planes (N residue planes + abs plane) of one operand image.
+inline size_t img_bytes(int rows, int k, int N) {
+  return (size_t)(N + 1) * align_up(ggemm_img_plane_bytes(rows, k), kAlign);
+}
+
+// Native FP64 groups for cublasDgemmGroupedBatched (host arrays, one entry per group).
+struct NativeGroups {
+  std::vector<cublasOperation_t> ta, tb;
+  std::vector<int> m, n, k, lda, ldb, ldc, size;
+  std::vector<double> alpha, beta;
+  void reserve(size_t P);
+};
+// Sorts idx[0..cnt) so problems with equal (m, n, k, lda, ldb, ldc, alpha, beta) are adjacent
+// and fills one group per run; returns the number of groups.
+int group_native(const ggemm_problem_t* probs, int* idx, int cnt, NativeGroups& g);
+
+// One chunk of emulated problems: descriptors live in the device blob at the given offsets.
+struct Chunk {
+  int first, count;        // range in emu order
+  size_t off_prep, off_prep_prefix, off_jobs, off_job_prefix, off_recon, off_recon_prefix;
+  int num_prep, prep_blocks;
+  long long tiles, recon_blocks;
+};
+
+}  // namespace g2
+
+struct ggemm_handle_s {
+  int device = 0, num_sms = 148;
+  cudaStream_t stream = nullptr;
+  cublasHandle_t cublas = nullptr;
+  void* cublas_ws = nullptr;
+  size_t cublas_ws_bytes = 0;
+
+  int max_problems = 0;
+  size_t max_A = 0, max_B = 0, max_C = 0;
+  int min_k = 32;
+
+  // device workspace (allocated at create; every call fits into it, in chunks if needed)
+  int8_t* imgA = nullptr;
+  size_t imgA_cap = 0;
+  int8_t* imgB = nullptr;
+  size_t imgB_cap = 0;
+  int32_t* c32 = nullptr;
+  size_t c32_cap = 0;  // int32 elements
+  int32_t* wsA = nullptr;
+  size_t wsA_cap = 0;
+  int32_t* wsB = nullptr;
+  size_t wsB_cap = 0;
+  g2::DevCounters* counters = nullptr;
+
+  // one pinned host descriptor blob per slot, mirrored by one device blob per slot
+  char* h_blob[2] = {nullptr, nullptr};
+  char* d_blob[2] = {nullptr, nullptr};
+  size_t blob_cap = 0;
+  cudaEvent_t slot_done[2] = {nullptr, nullptr};
+  int next_slot = 0;
+
+  // host scratch, sized at create (no allocation inside calls)
+  std::vector<g2::PlanEntry> plan;
+  std::vector<int> memo;
+  std::vector<int> emu, nat, order;
+  std::vector<int> ua_of, ub_of;          // per emulated problem: unique operand ids
+  std::vector<int> ua_rep, ub_rep, ua_n, ub_n;
+  std::vector<int> ua_chunk, ub_chunk;    // last chunk that prepped a unique operand
+  std::vector<size_t> ua_img, ub_img, ua_ws, ub_ws;
+  std::vector<size_t> c32_off;
+  std::vector<g2::Chunk> chunks;
+  g2::NativeGroups ngroups;
+  std::vector<const void*> nat_ptrs;
+
+  g2::DeviceModel dm{};
+  g2::ReuseArena reuse;
+  double rho_budget = 16.0;
+  int reuse_promote = 0;
+  int stats_repair = 0;
+  int ws_diag_printed = 0;
+};
+
+namespace g2 {
+// Validation shared by direct calls and plans (reference src/ggemm.cu:83-100).
+int validate_call(ggemm_handle_t h, const ggemm_problem_t* p, int num);
+// Public repair mode -> stage repair mode (-1 if invalid); default ON for AUTO, COUNT else.
+int stage_repair_mode(ggemm_path_t path, const ggemm_config_t* cfg);
+
+// Everything a call of the emulated grouped pipeline enqueues, prepared on the host.
+struct EmuCall {
+  int ne = 0, nn = 0, nprep_total = 0;
+  int nmax = 0, nmin = 0;
+  int num_ua = 0, num_ub = 0, num_promoted = 0;
+  bool reuse = false;
+  size_t blob_bytes = 0;
+  size_t off_nat_ptrs = 0;
+  int nat_groups = 0;
+};
+// Plans a call and writes every descriptor into host blob `hb`; the device addresses are
+// computed against `db`.  Returns GGEMM_OK or an error.
+int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cfg,
+                   const ggemm_problem_t* probs, int num, char* hb, const char* db,
+                   EmuCall* out);
+// Enqueues the launches of a built call on s (descriptors already on the device at db).
+// per_plane: EMU_LOOP (one GEMM launch per plane).
+int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* probs,
+                     const char* db, int repair, bool per_plane, cudaStream_t s,
+                     int* launches);
+int enqueue_native(ggemm_handle_t h, const ggemm_problem_t* probs, const int* idx, int cnt,
+                   bool grouped, int ngroups, const char* d_ptrs, cudaStream_t s, int* launches);
+}  // namespace g2

@@ -1,0 +1,845 @@
+// kernels.cu -- the three sm_100a kernels of the emulated grouped FP64 GEMM:
+//   prep_kernel   FP64 operands -> per-row power-of-two shifts, N int8 residue planes + the
+//                 abs plane, written directly in the tensor-core operand image layout
+//                 (ggemm_stages.h); HBM / integer-ALU bound.
+//   gemm_kernel   persistent tcgen05.mma.kind::i8 GEMM over every (problem, plane, tile):
+//                 bulk copies -> shared-memory ring (mbarriers) -> TMEM int32 accumulators ->
+//                 epilogue warps write int32 products; tensor-core bound.
+//   recon_kernel  CRT reconstruction, unscaling, alpha/beta, componentwise certificate and
+//                 FP64 repair; HBM bound.
+// The numerical definitions (what is computed, bit for bit) are those of the reference
+// src/ozaki2_numerics.cu:8-76 and :112-586; the work decomposition is this library's own.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+
+#include "crt.hpp"
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace g2 {
+
+__constant__ DevTables c_tab;
+
+// =============================================================================== shared math
+// x * 2^e: one multiplication for |e| <= 1000, else three clamped steps (the reference's
+// mul_pow2, src/ozaki2_numerics.cu:112-122; exact unless the result is subnormal).
+__device__ __forceinline__ double mul_pow2(double x, int e) {
+  if (e >= -1000 && e <= 1000) return x * __longlong_as_double((long long)(e + 1023) << 52);
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const int ee = max(-1000, min(1000, e));
+    x *= __longlong_as_double((long long)(ee + 1023) << 52);
+    e -= ee;
+  }
+  return x;
+}
+
+__device__ __forceinline__ bool needs_rescale(double maxabs) {
+  return maxabs > 0.0 && (maxabs > 0x1p400 || maxabs < 0x1p-400);
+}
+
+// Largest s with 2^s * ||x|| <= T (src/ozaki2_numerics.cu:133-153).
+__device__ __forceinline__ int shift_from_norm(double maxabs, double ssq, bool rescaled,
+                                               double T) {
+  if (isinf(maxabs) || isnan(ssq)) return kShiftNonfinite;
+  if (!(maxabs > 0.0)) return 0;
+  const double nm = sqrt(ssq * (1.0 + 0x1p-30));
+  int g, G;
+  const double f = frexp(nm, &g);
+  const double F = frexp(T, &G);
+  g += rescaled ? ilogb(maxabs) : 0;
+  return G - g - (f > F ? 1 : 0);
+}
+
+// Abs-plane exponent: maxabs * 2^sig in [64, 128) (src/ozaki2_numerics.cu:156-160).
+__device__ __forceinline__ int abs_shift(double maxabs, int sh) {
+  if (sh == kShiftNonfinite) return 0;
+  if (!(maxabs > 0.0)) return kShiftZero;
+  return 6 - ilogb(maxabs);
+}
+
+// Float upper bound of sqrt(x) as bits (src/ozaki2_numerics.cu:225-227).
+__device__ __forceinline__ int32_t norm_ub_bits(double x) {
+  return __float_as_int(__double2float_ru(sqrt(x * (1.0 + 0x1p-30))));
+}
+
+// ============================================================================== prep kernel
+// Residues.  For an integer-valued double x with |x| < 2^80, write |x| = sum_i d_i 2^(10 i)
+// (8 ten-bit digits).  For odd p:
+//     t = sum_i (+-d_i) * (2^(10 i) mod p)        |t| <= 8 * 1023 * 254 < 2^21: exact in FP32
+//     s = t - p * rint(t * fl(1/p))               exact symmetric residue of x mod p:
+// |t * fl(1/p) - t/p| <= 2^21/167 * 2^-24 + 2^-11 < 0.00125 while t/p is at least 1/(2p) >=
+// 0.00196 away from any half-integer (p odd), so rint picks round(t/p) and |s| <= (p-1)/2.
+// For p = 256 the residue is the low byte of x (negated for x < 0), read as int8.
+// The result is identical to the reference's Barrett / table evaluation
+// (src/ozaki2_numerics.cu:174-205): a residue class has exactly one symmetric representative.
+struct ElemDigits {
+  float f[kDigits];   // signed digits
+  uint32_t low;       // low byte of x (two's complement for x < 0)
+  bool wide;          // |x| >= 2^60: digits 6 and 7 in use
+};
+
+__device__ __forceinline__ void split_digits(double xt, ElemDigits& e) {
+  const uint64_t bits = (uint64_t)__double_as_longlong(xt);
+  const bool neg = (bits >> 63) != 0;
+  const int ex = (int)((bits >> 52) & 0x7FF);
+  uint64_t lo = 0, hi = 0;
+  if (ex >= 1023) {  // |x| >= 1 (x is an integer)
+    const uint64_t mant = (bits & 0xFFFFFFFFFFFFFull) | (1ull << 52);
+    const int sh = ex - 1075;  // |x| = mant * 2^sh, -52 <= sh <= 27
+    if (sh <= 0) {
+      lo = mant >> (-sh);
+    } else {
+      lo = mant << sh;
+      hi = mant >> (64 - sh);
+    }
+  }
+  const float sgn = neg ? -1.0f : 1.0f;
+  const float bias = neg ? 8388608.0f : -8388608.0f;
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    const uint32_t d = (uint32_t)(lo >> (10 * i)) & 1023u;
+    e.f[i] = fmaf(__uint_as_float(0x4B000000u | d), sgn, bias);
+  }
+  const uint32_t d6 = (uint32_t)((lo >> 60) | (hi << 4)) & 1023u;
+  const uint32_t d7 = (uint32_t)(hi >> 6) & 1023u;
+  e.f[6] = fmaf(__uint_as_float(0x4B000000u | d6), sgn, bias);
+  e.f[7] = fmaf(__uint_as_float(0x4B000000u | d7), sgn, bias);
+  e.wide = (hi | (lo >> 60)) != 0;
+  const uint32_t lb = (uint32_t)lo & 255u;
+  e.low = neg ? ((0u - lb) & 255u) : lb;
+}
+
+// Symmetric residue of x mod p_l (odd p) as the low byte of a 32-bit word.
+template <int D>
+__device__ __forceinline__ uint32_t odd_residue_byte(const ElemDigits& e, int l) {
+  float t = e.f[0];
+#pragma unroll
+  for (int i = 1; i < D; ++i) t = fmaf(e.f[i], c_tab.w[l][i], t);
+  const float q = rintf(t * c_tab.invpf[l]);
+  const float s = fmaf(-q, c_tab.pf[l], t);
+  return __float_as_uint(s + 12582912.0f);  // low byte = s mod 256 (|s| <= 127)
+}
+
+__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// Residue words of 4 elements for planes 0..N-1 into out[l].
+template <int D>
+__device__ __forceinline__ void residue_words4(const ElemDigits (&e)[4], int N,
+                                               uint32_t (&out)[kMaxModuli]) {
+  out[0] = pack4(e[0].low, e[1].low, e[2].low, e[3].low);
+#pragma unroll
+  for (int l = 1; l < kMaxModuli; ++l) {
+    if (l >= N) break;
+    out[l] = pack4(odd_residue_byte<D>(e[0], l), odd_residue_byte<D>(e[1], l),
+                   odd_residue_byte<D>(e[2], l), odd_residue_byte<D>(e[3], l));
+  }
+}
+
+// Abs-plane value floor(2^sg |a|) in [0, 127] (0 for an all-zero row).
+__device__ __forceinline__ uint32_t abs_byte(double a, int sg) {
+  if (sg == kShiftZero) return 0u;
+  const double v = fmin(127.0, trunc(mul_pow2(fabs(a), sg)));
+  return (uint32_t)__double_as_longlong(v + 4503599627370496.0) & 255u;
+}
+
+// trunc(2^sh a) (0 for rows / columns containing NaN or Inf).
+__device__ __forceinline__ double scaled_trunc(double a, int sh) {
+  if (sh == kShiftNonfinite) return 0.0;
+  return trunc(mul_pow2(a, sh));
+}
+
+// Image byte offset of (row r, K position q) inside a plane (ggemm_stages.h).
+__device__ __forceinline__ long long img_off(int rg, int r, int q) {
+  const int rr = r & 7, qq = q & 31;
+  return ((long long)(q >> 5) * rg + (r >> 3)) * 256 + rr * 32 + (((qq >> 4) ^ (rr >> 2)) << 4) +
+         (qq & 15);
+}
+
+struct PrepShared {
+  double a[8][32];
+  double b[8][32];
+  double rowmax[32];
+  int sh[32], sg[32];
+};
+
+// Rows of a column-major A: 32 rows per block, 8 warps.  Reduction orders (the reference's,
+// src/ozaki2_numerics.cu:263-364): for every row, 8 chains over K positions q = t (mod 8),
+// ascending, for the max / sum of squares and for ||dA||^2, ||A'||^2; chains combined
+// t = 0..7 from 0.0.
+__device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters* cnt,
+                                PrepShared& sm) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int rows = d.rows, K = d.k, N = d.N;
+  const int r = blk * 32 + lane;
+  const bool valid = r < rows;
+  const double* __restrict__ X = d.X;
+  const long long ld = d.ld;
+  const double T = c_tab.T[N];
+
+  double mx = 0.0, ss = 0.0;
+  if (valid)
+    for (int q = w; q < K; q += 8) {
+      const double a = X[r + q * ld];
+      mx = fmax(mx, fabs(a));
+      ss = fma(a, a, ss);
+    }
+  sm.a[w][lane] = mx;
+  __syncthreads();
+  if (w == 0) {
+    double M = 0.0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) M = fmax(M, sm.a[t][lane]);
+    sm.rowmax[lane] = M;
+  }
+  __syncthreads();
+  const double rowmax = sm.rowmax[lane];
+  const bool resc = valid && needs_rescale(rowmax);
+  if (resc) {  // rare: sum of squares of a * 2^-ilogb(rowmax)
+    const int e = -ilogb(rowmax);
+    ss = 0.0;
+    for (int q = w; q < K; q += 8) {
+      const double a = mul_pow2(X[r + q * ld], e);
+      ss = fma(a, a, ss);
+    }
+  }
+  sm.b[w][lane] = ss;
+  __syncthreads();
+  if (w == 0) {
+    double S = 0.0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) S += sm.b[t][lane];
+    const int sh = valid ? shift_from_norm(rowmax, S, resc, T) : 0;
+    const int sg = valid ? abs_shift(rowmax, sh) : kShiftZero;
+    sm.sh[lane] = sh;
+    sm.sg[lane] = sg;
+    if (valid) {
+      d.ws[r] = sh;
+      d.ws[rows + r] = sg;
+    }
+    const unsigned nf = __ballot_sync(0xFFFFFFFFu, valid && sh == kShiftNonfinite);
+    if (lane == 0 && nf) atomicAdd(&cnt->nonfinite, (unsigned long long)__popc(nf));
+  }
+  __syncthreads();
+  const int sh = sm.sh[lane], sg = sm.sg[lane];
+  const int ksteps = (K + 31) >> 5;
+  const int rg = (rows + 7) >> 3;
+  const bool in_image = (r >> 3) < rg;
+  const long long pb = d.plane_bytes;
+
+  double da = 0.0, na = 0.0;  // chain t = w
+  for (int k0 = 0; k0 < ksteps * 32; k0 += 64) {
+    // ||dA||^2, ||A'||^2 chains: q = k0 + w + 8 j (the reference's chain order)
+    if (sh != kShiftNonfinite) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int q = k0 + w + 8 * j;
+        const double a = (valid && q < K) ? X[r + q * ld] : 0.0;
+        const double xs = mul_pow2(a, sh);
+        const double xt = trunc(xs);
+        const double fr = xs - xt;
+        da = fma(fr, fr, da);
+        na = fma(xt, xt, na);
+      }
+    }
+    // residues of 8 consecutive K positions q0 .. q0+7 (8 bytes per plane)
+    const int q0 = k0 + 8 * w;
+    const bool store = in_image && (q0 >> 5) < ksteps;
+    ElemDigits e[2][4];
+    uint32_t absw[2];
+    bool wide = false;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      uint32_t ab[4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const int q = q0 + 4 * g + x;
+        const double a = (valid && q < K) ? X[r + q * ld] : 0.0;
+        split_digits(scaled_trunc(a, sh), e[g][x]);
+        ab[x] = (sh == kShiftNonfinite) ? 0u : abs_byte(a, sg);
+        wide |= e[g][x].wide;
+      }
+      absw[g] = pack4(ab[0], ab[1], ab[2], ab[3]);
+    }
+    uint32_t w0[kMaxModuli], w1[kMaxModuli];
+    if (__any_sync(0xFFFFFFFFu, wide)) {
+      residue_words4<8>(e[0], N, w0);
+      residue_words4<8>(e[1], N, w1);
+    } else {
+      residue_words4<6>(e[0], N, w0);
+      residue_words4<6>(e[1], N, w1);
+    }
+    if (store) {
+      int8_t* dst = d.img + img_off(rg, r, q0);
+#pragma unroll
+      for (int l = 0; l < kMaxModuli; ++l) {
+        if (l >= N) break;
+        *reinterpret_cast<uint2*>(dst + l * pb) = make_uint2(w0[l], w1[l]);
+      }
+      *reinterpret_cast<uint2*>(dst + N * pb) = make_uint2(absw[0], absw[1]);
+    }
+  }
+  __syncthreads();
+  sm.a[w][lane] = da;
+  sm.b[w][lane] = na;
+  __syncthreads();
+  if (w == 0 && valid) {
+    double D = 0.0, Nn = 0.0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      D += sm.a[t][lane];
+      Nn += sm.b[t][lane];
+    }
+    d.ws[2 * rows + r] = norm_ub_bits(D);
+    d.ws[3 * rows + r] = norm_ub_bits(Nn);
+  }
+}
+
+// Columns of a column-major B: one warp per column, 8 columns (one image row group) per
+// block.  Reduction orders (src/ozaki2_numerics.cu:368-441): max / sum of squares over lane
+// chains q = lane (mod 32); norms over lane chains q = 4 lane + 128 c + e; both combined by the
+// xor butterfly.
+__device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters* cnt) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int rows = d.rows, K = d.k, N = d.N;
+  const int col = blk * 8 + w;
+  const bool valid = col < rows;
+  const double* __restrict__ b = d.X + (long long)(valid ? col : 0) * d.ld;
+  const double T = c_tab.T[N];
+
+  double mx = 0.0, ss = 0.0;
+  if (valid)
+    for (int q = lane; q < K; q += 32) {
+      const double a = b[q];
+      mx = fmax(mx, fabs(a));
+      ss = fma(a, a, ss);
+    }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+  const bool resc = valid && needs_rescale(mx);
+  if (resc) {
+    const int e = -ilogb(mx);
+    ss = 0.0;
+    for (int q = lane; q < K; q += 32) {
+      const double a = mul_pow2(b[q], e);
+      ss = fma(a, a, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+  const int sh = valid ? shift_from_norm(mx, ss, resc, T) : 0;
+  const int sg = valid ? abs_shift(mx, sh) : kShiftZero;
+  if (valid && lane == 0) {
+    d.ws[col] = sh;
+    d.ws[rows + col] = sg;
+    if (sh == kShiftNonfinite) atomicAdd(&cnt->nonfinite, 1ull);
+  }
+  const int ksteps = (K + 31) >> 5;
+  const int rg = (rows + 7) >> 3;
+  const long long pb = d.plane_bytes;
+
+  double da = 0.0, na = 0.0;
+  for (int c0 = 0; c0 < ksteps * 32; c0 += 128) {
+    const int q0 = c0 + 4 * lane;
+    const bool in_k = (q0 >> 5) < ksteps;
+    ElemDigits e[4];
+    uint32_t ab[4];
+    bool wide = false;
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+      const int q = q0 + x;
+      const double a = (valid && q < K) ? b[q] : 0.0;
+      double xt = 0.0;
+      if (sh != kShiftNonfinite && in_k) {
+        const double xs = mul_pow2(a, sh);
+        xt = trunc(xs);
+        const double fr = xs - xt;
+        da = fma(fr, fr, da);
+        na = fma(xt, xt, na);
+      }
+      split_digits(xt, e[x]);
+      ab[x] = (sh == kShiftNonfinite) ? 0u : abs_byte(a, sg);
+      wide |= e[x].wide;
+    }
+    uint32_t wd[kMaxModuli];
+    if (__any_sync(0xFFFFFFFFu, wide))
+      residue_words4<8>(e, N, wd);
+    else
+      residue_words4<6>(e, N, wd);
+    if (in_k) {
+      int8_t* dst = d.img + img_off(rg, col, q0);
+#pragma unroll
+      for (int l = 0; l < kMaxModuli; ++l) {
+        if (l >= N) break;
+        *reinterpret_cast<uint32_t*>(dst + l * pb) = wd[l];
+      }
+      *reinterpret_cast<uint32_t*>(dst + N * pb) = pack4(ab[0], ab[1], ab[2], ab[3]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    da += __shfl_xor_sync(0xFFFFFFFFu, da, o);
+    na += __shfl_xor_sync(0xFFFFFFFFu, na, o);
+  }
+  if (valid && lane == 0) {
+    d.ws[2 * rows + col] = norm_ub_bits(da);
+    d.ws[3 * rows + col] = norm_ub_bits(na);
+  }
+}
+
+template <typename P>
+__device__ __forceinline__ int find_owner(const P* __restrict__ prefix, int num, P x) {
+  int lo = 0, hi = num - 1;  // largest i with prefix[i] <= x
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= x) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const ggemm_prep_desc_t* __restrict__ descs,
+                                                            const int* __restrict__ prefix,
+                                                            int num, DevCounters* cnt) {
+  __shared__ PrepShared sm;
+  const int owner = find_owner(prefix, num, (int)blockIdx.x);
+  const ggemm_prep_desc_t d = descs[owner];
+  if (d.N < 1 || d.N > kMaxModuli || d.rows <= 0) return;
+  const int blk = (int)blockIdx.x - prefix[owner];
+  if (d.kind == 0) prep_rows_block(d, blk, cnt, sm);
+  else prep_cols_block(d, blk, cnt);
+}
+
+// ============================================================================== GEMM kernel
+// Tile 128 x 128 x (4 x 32-byte K steps) per pipeline stage.  Warp roles:
+//   warp 0: TMEM allocation + bulk-copy producer (one lane)
+//   warp 1: tcgen05.mma issuer (one lane)
+//   warps 2..5: epilogue (TMEM -> registers -> int32 stores); warp w reads TMEM lanes
+//   32 (w % 4) .. 32 (w % 4) + 31, i.e. tile rows.
+// Two TMEM accumulators (2 x 128 columns) let the epilogue of one tile overlap the MMAs of the
+// next.  Tiles are handed out statically (tile t to CTA t mod grid) from a host-side LPT order.
+constexpr int kStages = 6;
+constexpr int kStepBytes = 16 * 256;            // one 32-byte K step of 128 rows
+constexpr int kStageBytes = 2 * 4 * kStepBytes;  // A + B, 4 K steps each
+constexpr int kGemmThreads = 192;
+constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
+
+struct GemmSmemCtl {
+  uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], drain;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + sizeof(GemmSmemCtl) + 64;
+
+struct TileInfo {
+  const GemmJob* job;
+  int plane, tm, tn;
+};
+
+__device__ __forceinline__ TileInfo decode_tile(const GemmJob* __restrict__ jobs,
+                                                const long long* __restrict__ prefix, int num,
+                                                long long t) {
+  TileInfo ti;
+  const int j = find_owner(prefix, num, t);
+  ti.job = jobs + j;
+  const long long local = t - prefix[j];
+  const int per_plane = ti.job->tm * ti.job->tn;
+  ti.plane = (int)(local / per_plane);
+  const int rem = (int)(local - (long long)ti.plane * per_plane);
+  ti.tn = rem / ti.job->tm;
+  ti.tm = rem - ti.tn * ti.job->tm;
+  return ti;
+}
+
+__device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, GemmSmemCtl* ctl,
+                                             DevCounters* cnt) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t deadline = global_timer_ns() + kWaitNs;
+  if (mbar_wait(bar, parity, deadline, &ctl->abort)) return true;
+  ctl->abort = 1;
+  atomicCAS(&cnt->status, 0u, (unsigned)kStatusGemmTimeout);
+  return false;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const GemmJob* __restrict__ jobs, const long long* __restrict__ prefix, int num,
+                long long total_tiles, DevCounters* cnt) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  GemmSmemCtl* ctl = reinterpret_cast<GemmSmemCtl*>(smem + kStages * kStageBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->acc_full[b], 1);
+      mbar_init(&ctl->acc_empty[b], 4);
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&ctl->tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0, last_par = 0;  // per stage: ever armed / parity of the last arming
+      for (long long t = blockIdx.x; t < total_tiles && !ctl->abort; t += gridDim.x) {
+        const TileInfo ti = decode_tile(jobs, prefix, num, t);
+        const GemmJob& jb = *ti.job;
+        const int g0a = ti.tm * 16, ga = min(16, jb.rga - g0a);
+        const int g0b = ti.tn * 16, gb = min(16, jb.rgb - g0b);
+        const int8_t* A = jb.A + (long long)ti.plane * jb.a_plane + (long long)g0a * 256;
+        const int8_t* B = jb.B + (long long)ti.plane * jb.b_plane + (long long)g0b * 256;
+        const long long astep = (long long)jb.rga * 256, bstep = (long long)jb.rgb * 256;
+        for (int ks = 0; ks < jb.ksteps; ks += 4) {
+          const int nst = min(4, jb.ksteps - ks);
+          if (!bounded_wait(&ctl->empty[stage], phase ^ 1u, ctl, cnt)) break;
+          mbar_arrive_expect_tx(&ctl->full[stage], (uint32_t)(nst * (ga + gb) * 256));
+          armed |= 1u << stage;
+          last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          uint8_t* sa = smem + stage * kStageBytes;
+          uint8_t* sb = sa + 4 * kStepBytes;
+          for (int j = 0; j < nst; ++j) {
+            bulk_g2s(sa + j * kStepBytes, A + (long long)(ks + j) * astep, (uint32_t)(ga * 256),
+                     &ctl->full[stage]);
+            bulk_g2s(sb + j * kStepBytes, B + (long long)(ks + j) * bstep, (uint32_t)(gb * 256),
+                     &ctl->full[stage]);
+          }
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // every issued copy has landed before the CTA may exit
+      for (int s = 0; s < kStages; ++s)
+        if (armed & (1u << s)) {
+          const uint64_t deadline = global_timer_ns() + kWaitNs;
+          int dummy_abort = 0;
+          mbar_wait(&ctl->full[s], (last_par >> s) & 1u, deadline, &dummy_abort);
+        }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc = idesc_i8(kGemmBM, kGemmBN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int buf = 0;
+      uint32_t acc_phase = 0;
+      bool issued = false;
+      for (long long t = blockIdx.x; t < total_tiles && !ctl->abort; t += gridDim.x) {
+        const TileInfo ti = decode_tile(jobs, prefix, num, t);
+        const int ksteps = ti.job->ksteps;
+        if (!bounded_wait(&ctl->acc_empty[buf], acc_phase ^ 1u, ctl, cnt)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(buf * kGemmBN);
+        bool ok = true;
+        for (int ks = 0; ks < ksteps; ks += 4) {
+          const int nst = min(4, ksteps - ks);
+          if (!bounded_wait(&ctl->full[stage], phase, ctl, cnt)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_addr(smem + stage * kStageBytes);
+          const uint32_t sb = sa + 4 * kStepBytes;
+          for (int j = 0; j < nst; ++j) {
+            const uint64_t ad = smem_desc_sw32(sa + j * kStepBytes, 256);
+            const uint64_t bd = smem_desc_sw32(sb + j * kStepBytes, 256);
+            mma_i8(d_tmem, ad, bd, idesc, (ks > 0 || j > 0) ? 1u : 0u);
+          }
+          issued = true;
+          mma_commit(&ctl->empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&ctl->acc_full[buf]);
+        if (++buf == 2) {
+          buf = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (issued) {  // all MMAs of this CTA complete before TMEM is released
+        mma_commit(&ctl->drain);
+        const uint64_t deadline = global_timer_ns() + kWaitNs;
+        int dummy_abort = 0;
+        mbar_wait(&ctl->drain, 0, deadline, &dummy_abort);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    int buf = 0;
+    uint32_t acc_phase = 0;
+    for (long long t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const TileInfo ti = decode_tile(jobs, prefix, num, t);
+      const GemmJob& jb = *ti.job;
+      bool ok = true;
+      if (lane == 0) ok = bounded_wait(&ctl->acc_full[buf], acc_phase, ctl, cnt);
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = ti.tm * kGemmBM + quad * 32 + lane;
+      int32_t* C = jb.C + (long long)ti.plane * jb.c_plane;
+      const uint32_t taddr = tmem + (uint32_t)(buf * kGemmBN) + ((uint32_t)(quad * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kGemmBN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
+        tmem_ld_wait();
+        const int col0 = ti.tn * kGemmBN + c * 32;
+        if (row < jb.m) {
+          int32_t* cp = C + row + (long long)col0 * jb.m;
+          const int ncol = min(32, jb.n - col0);
+#pragma unroll
+          for (int x = 0; x < 32; ++x)
+            if (x < ncol) cp[(long long)x * jb.m] = (int32_t)v[x];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->acc_empty[buf]);
+      if (++buf == 2) {
+        buf = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ======================================================================= reconstruct kernel
+// y mod p for 0 <= y < 2^32, magic = floor(2^32 / p): the estimate undershoots by at most one.
+__device__ __forceinline__ uint32_t mod_p(uint32_t y, uint32_t p, uint32_t magic) {
+  const uint32_t q = __umulhi(y, magic);
+  const uint32_t r = y - q * p;
+  return r >= p ? r - p : r;
+}
+
+// Sequential fma dot product over k (src/ozaki2_numerics.cu:445-452): the same rounding as a
+// native FP64 dot, used for repairs and for rows / columns containing NaN or Inf.
+__device__ __forceinline__ double fp64_dot(const ggemm_recon_desc_t& d, int i, int j) {
+  const double* a = d.A + i;
+  const double* b = d.B + (long long)j * d.ldb;
+  double s = 0.0;
+  for (int q = 0; q < d.k; ++q) s = fma(a[(long long)q * d.lda], b[q], s);
+  return s;
+}
+
+// One output entry (src/ozaki2_numerics.cu:485-563): returns the value and bumps the counters.
+__device__ __forceinline__ void recon_entry(const ggemm_recon_desc_t& d, int mode, long long idx,
+                                            int i, int j, unsigned& n_unc, unsigned& n_rep,
+                                            unsigned& n_saf) {
+  const int N = d.N;
+  double* cp = d.C + i + (long long)j * d.ldc;
+  const double alpha = d.alpha, beta = d.beta;
+  const double c0 = (beta == 0.0) ? 0.0 : *cp;
+  if (alpha == 0.0) {
+    *cp = (beta == 0.0) ? 0.0 : beta * c0;
+    return;
+  }
+  const int rsh = d.rs[i], csh = d.cs[j];
+  if (rsh == kShiftNonfinite || csh == kShiftNonfinite) {
+    const double v = fp64_dot(d, i, j);
+    *cp = (beta == 0.0) ? alpha * v : fma(alpha, v, beta * c0);
+    ++n_saf;
+    return;
+  }
+  const int sig = d.rs[d.m + i], tau = d.cs[d.n + j];
+  if (sig == kShiftZero || tau == kShiftZero) {
+    *cp = (beta == 0.0) ? alpha * 0.0 : fma(alpha, 0.0, beta * c0);
+    return;
+  }
+  const int32_t* __restrict__ C32 = d.C32 + idx;
+  const long long cst = d.c_plane;
+  uint64_t S1 = 0;
+  uint32_t S2 = 0;
+#pragma unroll 4
+  for (int l = 0; l < N; ++l) {
+    const uint32_t p = c_tab.p[l], mg = c_tab.magic[l];
+    const int32_t c = __ldg(C32 + l * cst);
+    const uint32_t uc = c < 0 ? 0u - (uint32_t)c : (uint32_t)c;
+    uint32_t r = mod_p(uc, p, mg);
+    if (c < 0 && r) r = p - r;
+    const uint32_t y = mod_p(r * c_tab.qinv[N][l], p, mg);
+    S1 += c_tab.s1[N][l] * (uint64_t)y;
+    S2 += c_tab.s2[N][l] * y;
+  }
+  const double s2d = (double)S2 * 0x1p-18;
+  const double Q = rint(((double)S1 + s2d) * c_tab.inv_Pu[N]);
+  const long long X1 = (long long)S1 - (long long)Q * c_tab.P1[N];
+  const double xr = (double)X1 + fma(-Q, c_tab.P2[N], s2d);
+  const int lu1 = c_tab.log2_u1[N];
+  const int esc = lu1 - rsh - csh;
+  const double v = mul_pow2(xr, esc);
+  const double emu = (beta == 0.0) ? alpha * v : fma(alpha, v, beta * c0);
+  if (mode == GGEMM_STAGE_REPAIR_OFF || (beta != 0.0 && !isfinite(c0))) {
+    *cp = emu;
+    return;
+  }
+  // certificate: rigorous error bound E vs gamma_n (|alpha| lower(|A||B|) + |beta C0|)
+  const double u = 0x1p-53;
+  const double nt = (double)d.k + (alpha != 1.0 ? 1.0 : 0.0) + (beta != 0.0 ? 1.0 : 0.0);
+  const double gam = (nt * u / fma(-nt, u, 1.0) - 2.0 * u) * (1.0 - 0x1p-40);
+  const double crt_u = N * 255.0 * 0x1p-19 + 0x1p-10;
+  const double da = __int_as_float(d.rs[2 * d.m + i]), na = __int_as_float(d.rs[3 * d.m + i]);
+  const double db = __int_as_float(d.cs[2 * d.n + j]), nb = __int_as_float(d.cs[3 * d.n + j]);
+  const double et = fma(da, nb, fma(na, db, da * db)) * (1.0 + 0x1p-40);
+  const double inv_u1 = __longlong_as_double((long long)(1023 - lu1) << 52);
+  const double Eu = fma(4.0 * u, fabs(xr), fma(et, inv_u1, crt_u)) * (1.0 + 0x1p-40);
+  const double E = mul_pow2(Eu, esc);
+  const double L = (double)__ldg(C32 + N * cst);
+  double lab = mul_pow2(L, -(sig + tau));
+  lab = fmax(lab, fabs(v) - E) * (1.0 - 0x1p-40);
+  if (lab < 0x1p-1000) lab = 0.0;
+  const double aalpha = fabs(alpha);
+  const double lhs = aalpha * E * (1.0 + 0x1p-40);
+  const double rhs = gam * fma(aalpha, lab, fabs(beta * c0)) * (1.0 - 0x1p-40);
+  const bool cert = gam > 0.0 && E >= 0x1p-1000 && isfinite(lhs) && isfinite(v) && lhs <= rhs;
+  if (cert) {
+    *cp = emu;
+  } else if (mode == GGEMM_STAGE_REPAIR_COUNT) {
+    *cp = emu;
+    ++n_unc;
+  } else {
+    const double r = fp64_dot(d, i, j);
+    *cp = (beta == 0.0) ? alpha * r : fma(alpha, r, beta * c0);
+    ++n_rep;
+  }
+}
+
+__global__ void __launch_bounds__(kReconThreads) recon_kernel(const ggemm_recon_desc_t* __restrict__ descs,
+                                                              const long long* __restrict__ prefix,
+                                                              int num, int mode,
+                                                              DevCounters* cnt) {
+  const int owner = find_owner(prefix, num, (long long)blockIdx.x);
+  const ggemm_recon_desc_t d = descs[owner];
+  unsigned n_unc = 0, n_rep = 0, n_saf = 0;
+  if (d.N >= 1 && d.N <= kMaxModuli && d.m > 0 && d.n > 0) {
+    const long long mn = (long long)d.m * d.n;
+    const long long base = ((long long)blockIdx.x - prefix[owner]) * (kReconThreads * kReconPerThread);
+#pragma unroll 1
+    for (int e = 0; e < kReconPerThread; ++e) {
+      const long long idx = base + e * kReconThreads + threadIdx.x;
+      if (idx >= mn) break;
+      const int j = (int)(idx / d.m);
+      const int i = (int)(idx - (long long)j * d.m);
+      recon_entry(d, mode, idx, i, j, n_unc, n_rep, n_saf);
+    }
+  }
+  // counters: warp reduce, block reduce, at most one atomic per counter per block
+  unsigned long long cu = n_unc, cr = n_rep, cf = n_saf;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    cu += __shfl_xor_sync(0xFFFFFFFFu, cu, o);
+    cr += __shfl_xor_sync(0xFFFFFFFFu, cr, o);
+    cf += __shfl_xor_sync(0xFFFFFFFFu, cf, o);
+  }
+  __shared__ unsigned long long s_cnt[3][kReconThreads / 32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) {
+    s_cnt[0][w] = cu;
+    s_cnt[1][w] = cr;
+    s_cnt[2][w] = cf;
+  }
+  __syncthreads();
+  if (threadIdx.x < 3) {
+    unsigned long long t = 0;
+    for (int x = 0; x < kReconThreads / 32; ++x) t += s_cnt[threadIdx.x][x];
+    if (t) {
+      unsigned long long* dst = threadIdx.x == 0 ? &cnt->uncertified
+                                : threadIdx.x == 1 ? &cnt->repaired
+                                                   : &cnt->safety;
+      atomicAdd(dst, t);
+    }
+  }
+}
+
+// ===================================================================================== host
+namespace {
+std::mutex g_dev_mu;
+uint64_t g_uploaded = 0;  // bit per device ordinal (< 64)
+int g_sms[64] = {0};
+bool g_gemm_attr[64] = {false};
+}  // namespace
+
+int upload_tables_current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (g_uploaded & (1ull << dev)) return 0;
+  int st = 0;
+  const CrtTables& t = crt_tables(&st);
+  if (st != 0) return 100 + st;
+  static DevTables dt;
+  make_dev_tables(t, &dt);
+  if (cudaMemcpyToSymbol(c_tab, &dt, sizeof(dt)) != cudaSuccess) return 2;
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  g_sms[dev] = sms > 0 ? sms : 148;
+  if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kGemmSmem) != cudaSuccess)
+    return 3;
+  g_gemm_attr[dev] = true;
+  if (cudaDeviceSynchronize() != cudaSuccess) return 4;
+  g_uploaded |= 1ull << dev;
+  return 0;
+}
+
+int current_device_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  return g_sms[dev] > 0 ? g_sms[dev] : 148;
+}
+
+int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, int num, int total_blocks,
+                DevCounters* cnt, cudaStream_t s) {
+  if (num <= 0 || total_blocks <= 0) return 0;
+  prep_kernel<<<total_blocks, kPrepThreads, 0, s>>>(d_descs, d_prefix, num, cnt);
+  return (int)cudaGetLastError();
+}
+
+int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long long total_tiles,
+                DevCounters* cnt, cudaStream_t s) {
+  if (num <= 0 || total_tiles <= 0) return 0;
+  const long long grid = std::min<long long>(total_tiles, (long long)current_device_sms());
+  gemm_kernel<<<(unsigned)grid, kGemmThreads, kGemmSmem, s>>>(d_jobs, d_prefix, num, total_tiles,
+                                                              cnt);
+  return (int)cudaGetLastError();
+}
+
+int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix, int num,
+                 long long total_blocks, int mode, DevCounters* cnt, cudaStream_t s) {
+  if (num <= 0 || total_blocks <= 0) return 0;
+  if (total_blocks > 0x7FFFFFFFLL) return (int)cudaErrorInvalidConfiguration;
+  recon_kernel<<<(unsigned)total_blocks, kReconThreads, 0, s>>>(d_descs, d_prefix, num, mode, cnt);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace g2

@@ -1,0 +1,217 @@
+// stages.cpp -- ggemm_stage_* entry points (include/ggemm_stages.h): each stage of the
+// pipeline as one kernel launch over caller-provided buffers, for parity tests.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "internal.hpp"
+
+using namespace g2;
+
+namespace {
+
+// Host staging for the descriptor copy.  cudaMemcpyAsync from pageable memory returns only
+// after the source has been consumed, so the buffer may be reused by the next call.
+thread_local std::vector<char> t_stage;
+
+size_t blob_layout(int num, size_t desc_bytes, size_t prefix_elem, size_t* off_prefix) {
+  *off_prefix = align_up((size_t)num * desc_bytes, 64);
+  return *off_prefix + (size_t)(num + 1) * prefix_elem;
+}
+
+int copy_blob(void* scratch, size_t scratch_bytes, size_t bytes, cudaStream_t s) {
+  if (bytes > scratch_bytes) return GGEMM_ERR_WORKSPACE;
+  return cudaMemcpyAsync(scratch, t_stage.data(), bytes, cudaMemcpyHostToDevice, s) ==
+                 cudaSuccess
+             ? GGEMM_OK
+             : GGEMM_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" size_t ggemm_stage_scratch_bytes(int num) {
+  const size_t d = std::max({sizeof(ggemm_prep_desc_t), sizeof(GemmJob),
+                             sizeof(ggemm_recon_desc_t)});
+  return align_up((size_t)std::max(num, 1) * d, 64) + (size_t)(num + 2) * 8 + 256;
+}
+
+extern "C" int ggemm_stage_prep(const ggemm_prep_desc_t* descs, int num, void* scratch,
+                                size_t scratch_bytes, void* counters, cudaStream_t s) {
+  if (num < 0 || (num > 0 && (!descs || !scratch || !counters))) return GGEMM_ERR_INVALID;
+  if (num == 0) return GGEMM_OK;
+  if (upload_tables_current_device()) return GGEMM_ERR_NUMERICS;
+  size_t off_p;
+  const size_t bytes = blob_layout(num, sizeof(ggemm_prep_desc_t), sizeof(int), &off_p);
+  t_stage.assign(bytes, 0);
+  std::memcpy(t_stage.data(), descs, (size_t)num * sizeof(ggemm_prep_desc_t));
+  int* pre = reinterpret_cast<int*>(t_stage.data() + off_p);
+  long long blocks = 0;
+  for (int i = 0; i < num; ++i) {
+    const ggemm_prep_desc_t& d = descs[i];
+    if (d.rows < 0 || d.k < 0 || d.N < 1 || d.N > kMaxModuli || (d.kind != 0 && d.kind != 1))
+      return GGEMM_ERR_INVALID;
+    if (d.rows > 0 && (!d.X || !d.img || !d.ws)) return GGEMM_ERR_INVALID;
+    if (((uintptr_t)d.img & 15) || (d.plane_bytes & 15) ||
+        (size_t)d.plane_bytes < ggemm_img_plane_bytes(d.rows, d.k))
+      return GGEMM_ERR_INVALID;
+    pre[i] = (int)blocks;
+    blocks += prep_blocks(d);
+    if (blocks > 0x7FFFFFFF) return GGEMM_ERR_INVALID;
+  }
+  pre[num] = (int)blocks;
+  int r = copy_blob(scratch, scratch_bytes, bytes, s);
+  if (r) return r;
+  const char* db = static_cast<const char*>(scratch);
+  return launch_prep(reinterpret_cast<const ggemm_prep_desc_t*>(db),
+                     reinterpret_cast<const int*>(db + off_p), num, (int)blocks,
+                     static_cast<DevCounters*>(counters), s)
+             ? GGEMM_ERR_NUMERICS
+             : GGEMM_OK;
+}
+
+extern "C" int ggemm_stage_gemm(const ggemm_gemm_desc_t* descs, int num, void* scratch,
+                                size_t scratch_bytes, void* counters, cudaStream_t s) {
+  if (num < 0 || (num > 0 && (!descs || !scratch || !counters))) return GGEMM_ERR_INVALID;
+  if (num == 0) return GGEMM_OK;
+  if (upload_tables_current_device()) return GGEMM_ERR_I8GEMM;
+  size_t off_p;
+  const size_t bytes = blob_layout(num, sizeof(GemmJob), sizeof(long long), &off_p);
+  t_stage.assign(bytes, 0);
+  GemmJob* jobs = reinterpret_cast<GemmJob*>(t_stage.data());
+  long long* pre = reinterpret_cast<long long*>(t_stage.data() + off_p);
+  long long tiles = 0;
+  for (int i = 0; i < num; ++i) {
+    const ggemm_gemm_desc_t& d = descs[i];
+    if (d.m < 0 || d.n < 0 || d.k < 0 || d.planes < 0 || d.k > kMaxKExact)
+      return GGEMM_ERR_INVALID;
+    GemmJob j{};
+    j.A = d.A;
+    j.B = d.B;
+    j.C = d.C;
+    j.a_plane = d.a_plane;
+    j.b_plane = d.b_plane;
+    j.c_plane = d.c_plane;
+    j.m = d.m;
+    j.n = d.n;
+    j.ksteps = (d.k + 31) / 32;
+    j.planes = (d.m > 0 && d.n > 0 && d.k > 0) ? d.planes : 0;
+    j.rga = (d.m + 7) / 8;
+    j.rgb = (d.n + 7) / 8;
+    j.tm = (d.m + kGemmBM - 1) / kGemmBM;
+    j.tn = (d.n + kGemmBN - 1) / kGemmBN;
+    if (j.planes > 0) {
+      if (!d.A || !d.B || !d.C || ((uintptr_t)d.A & 15) || ((uintptr_t)d.B & 15) ||
+          ((uintptr_t)d.C & 3) || (d.a_plane & 15) || (d.b_plane & 15))
+        return GGEMM_ERR_INVALID;
+      if ((size_t)d.a_plane < ggemm_img_plane_bytes(d.m, d.k) ||
+          (size_t)d.b_plane < ggemm_img_plane_bytes(d.n, d.k) ||
+          d.c_plane < (long long)d.m * d.n)
+        return GGEMM_ERR_INVALID;
+    }
+    jobs[i] = j;
+    pre[i] = tiles;
+    tiles += gemm_tiles(j);
+  }
+  pre[num] = tiles;
+  int r = copy_blob(scratch, scratch_bytes, bytes, s);
+  if (r) return r;
+  const char* db = static_cast<const char*>(scratch);
+  return launch_gemm(reinterpret_cast<const GemmJob*>(db),
+                     reinterpret_cast<const long long*>(db + off_p), num, tiles,
+                     static_cast<DevCounters*>(counters), s)
+             ? GGEMM_ERR_I8GEMM
+             : GGEMM_OK;
+}
+
+extern "C" int ggemm_stage_recon(const ggemm_recon_desc_t* descs, int num, int repair_mode,
+                                 void* scratch, size_t scratch_bytes, void* counters,
+                                 cudaStream_t s) {
+  if (num < 0 || (num > 0 && (!descs || !scratch || !counters))) return GGEMM_ERR_INVALID;
+  if (repair_mode < GGEMM_STAGE_REPAIR_OFF || repair_mode > GGEMM_STAGE_REPAIR_ON)
+    return GGEMM_ERR_INVALID;
+  if (num == 0) return GGEMM_OK;
+  if (upload_tables_current_device()) return GGEMM_ERR_NUMERICS;
+  size_t off_p;
+  const size_t bytes = blob_layout(num, sizeof(ggemm_recon_desc_t), sizeof(long long), &off_p);
+  t_stage.assign(bytes, 0);
+  std::memcpy(t_stage.data(), descs, (size_t)num * sizeof(ggemm_recon_desc_t));
+  long long* pre = reinterpret_cast<long long*>(t_stage.data() + off_p);
+  long long blocks = 0;
+  for (int i = 0; i < num; ++i) {
+    const ggemm_recon_desc_t& d = descs[i];
+    if (d.m < 0 || d.n < 0 || d.k < 0 || d.N < 1 || d.N > kMaxModuli) return GGEMM_ERR_INVALID;
+    pre[i] = blocks;
+    blocks += recon_blocks(d);
+  }
+  pre[num] = blocks;
+  int r = copy_blob(scratch, scratch_bytes, bytes, s);
+  if (r) return r;
+  const char* db = static_cast<const char*>(scratch);
+  return launch_recon(reinterpret_cast<const ggemm_recon_desc_t*>(db),
+                      reinterpret_cast<const long long*>(db + off_p), num, blocks, repair_mode,
+                      static_cast<DevCounters*>(counters), s)
+             ? GGEMM_ERR_NUMERICS
+             : GGEMM_OK;
+}
+
+extern "C" int ggemm_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+extern "C" const char* ggemm_version(void) { return "ggemm-b200 0.1 (sm_100a)"; }
+
+extern "C" int ggemm_stage_plan(const ggemm_problem_t* problems, int num,
+                                const ggemm_config_t* cfg, int path, int num_sms,
+                                double fp64_flops, double int8_ops, double mem_bw,
+                                double tiny_mnk, double rho_budget, int* route,
+                                int* num_moduli, int* tile_cfg) {
+  if (num < 0 || (num > 0 && (!problems || !route || !num_moduli || !tile_cfg)))
+    return GGEMM_ERR_INVALID;
+  DeviceModel dm{num_sms, fp64_flops, int8_ops, mem_bw, tiny_mnk};
+  std::vector<PlanEntry> out((size_t)std::max(num, 1));
+  const int r = plan_group(problems, num, cfg, (ggemm_path_t)path, dm,
+                           rho_budget > 0 ? rho_budget : env_rho_budget(), out.data(), nullptr,
+                           0);
+  if (r) return r;
+  for (int g = 0; g < num; ++g) {
+    route[g] = out[g].route;
+    num_moduli[g] = out[g].num_moduli;
+    tile_cfg[g] = out[g].tile_cfg;
+  }
+  return GGEMM_OK;
+}
+
+extern "C" int ggemm_stage_reuse(const ggemm_problem_t* problems, int num, const int* nmod,
+                                 int policy, int* out) {
+  if (num < 0 || !out) return GGEMM_ERR_INVALID;
+  ReuseArena ar;
+  if (ar.reserve(std::max(num, 1))) return GGEMM_ERR_INVALID;
+  const ReuseResult r =
+      ar.build(problems, num, nmod, policy == 1 ? kReusePromote : kReuseExactN);
+  if (r.status) return r.status == 1 ? GGEMM_ERR_WORKSPACE : GGEMM_ERR_INVALID;
+  out[0] = r.num_ua;
+  out[1] = r.num_ub;
+  out[2] = r.num_promoted;
+  int* o = out + 3;
+  for (int i = 0; i < num; ++i) o[i] = i < r.num_ua ? r.ua_rep[i] : -1;
+  o += num;
+  for (int i = 0; i < num; ++i) o[i] = i < r.num_ua ? r.ua_nmod[i] : 0;
+  o += num;
+  for (int i = 0; i < num; ++i) o[i] = i < r.num_ub ? r.ub_rep[i] : -1;
+  o += num;
+  for (int i = 0; i < num; ++i) o[i] = i < r.num_ub ? r.ub_nmod[i] : 0;
+  o += num;
+  for (int i = 0; i < num; ++i) o[i] = r.prob_a[i];
+  o += num;
+  for (int i = 0; i < num; ++i) o[i] = r.prob_b[i];
+  o += num;
+  for (int i = 0; i < num; ++i) o[i] = r.eff_nmod[i];
+  return GGEMM_OK;
+}

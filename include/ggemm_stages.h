@@ -1,0 +1,128 @@
+/* ggemm_stages.h -- stage-level entry points of the emulation pipeline (parity seams).
+ *
+ * The reference exposes its three stages as internal C++ functions that its own tests call
+ * one by one (src/ozaki2_numerics.h:39-105 and src/int8_grouped_gemm.h:34-101).  These are the
+ * same seams as a plain C ABI, so a test can run prep, the residue GEMM and the reconstruct
+ * separately and compare residues, int32 products and outputs with a checker:
+ *   ggemm_stage_prep    replaces oz2_prep_grouped          (src/ozaki2_numerics.cu:609-623)
+ *   ggemm_stage_gemm    replaces i8_grouped_gemm / _launch (src/int8_grouped_gemm.cu:711-780)
+ *   ggemm_stage_recon   replaces oz2_reconstruct_grouped   (src/ozaki2_numerics.cu:625-637)
+ *   ggemm_stage_counters_* replace oz2_read_counters       (src/ozaki2_numerics.cu:675-693)
+ *
+ * Residue planes are stored in this library's own layout: each plane is the image of a K-major
+ * tensor-core operand with 32-byte swizzle, so the GEMM fetches a tile with one bulk copy per
+ * 32-byte K step:
+ *   rows are grouped by 8 (row group g = r / 8), K by 32 bytes (step s = q / 32);
+ *   atom (s, g) = 256 contiguous bytes at ((s * RG) + g) * 256, RG = ceil(rows / 8);
+ *   inside an atom, row r % 8 occupies 32 bytes at (r % 8) * 32, its two 16-byte halves
+ *   swapped when bit 2 of (r % 8) is set:  byte (q % 32) lands at
+ *   (((q % 32) / 16) ^ ((r % 8) >> 2)) * 16 + (q % 16).
+ * Rows r >= rows (up to RG*8) and K positions q >= k (up to ceil(k/32)*32) hold zeros.
+ */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#include "ggemm.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GGEMM_IMG_GROUP_ROWS 8
+#define GGEMM_IMG_KSTEP 32
+#define GGEMM_IMG_ATOM 256
+
+/* Bytes of one residue plane of a rows x k operand. */
+static inline size_t ggemm_img_plane_bytes(int rows, int k) {
+  const size_t rg = ((size_t)rows + 7) / 8, ks = ((size_t)k + 31) / 32;
+  return rg * ks * GGEMM_IMG_ATOM;
+}
+/* Byte offset of element (r, q) inside a plane of an operand with `rows` rows. */
+static inline size_t ggemm_img_offset(int rows, int r, int q) {
+  const size_t rg = ((size_t)rows + 7) / 8;
+  const int rr = r & 7, qq = q & 31;
+  return ((size_t)(q >> 5) * rg + (size_t)(r >> 3)) * GGEMM_IMG_ATOM + (size_t)rr * 32 +
+         (size_t)(((qq >> 4) ^ (rr >> 2)) * 16 + (qq & 15));
+}
+
+/* One operand of one problem for prep.  kind 0: the rows of a column-major A (element (r, q)
+ * at X[r + q*ld]); kind 1: the columns of a column-major B (element (r, q) at X[q + r*ld]).
+ * img: N+1 planes (N residue planes, then the abs plane) at stride plane_bytes.
+ * ws: 4*rows int32 {shift | abs shift | ||dX_r|| (float bits) | ||X'_r|| (float bits)}. */
+typedef struct {
+  const double* X;
+  long long ld;
+  int rows, k, N, kind;
+  int8_t* img;
+  long long plane_bytes;
+  int32_t* ws;
+} ggemm_prep_desc_t;
+
+/* One problem of the residue GEMM: for every plane l < planes,
+ * C[l*c_plane + i + j*m] = sum_q A_l(i, q) * B_l(j, q) (exact int32), A/B in the image
+ * layout above (A: m rows, B: n rows, depth k). */
+typedef struct {
+  const int8_t* A;
+  const int8_t* B;
+  int32_t* C;
+  long long a_plane, b_plane, c_plane; /* bytes, bytes, int32 elements */
+  int m, n, k, planes;
+} ggemm_gemm_desc_t;
+
+/* One problem of the reconstruct.  C32: N+1 planes of m*n int32 (column-major, ld = m) at
+ * stride c_plane elements; rs / cs: prep workspaces of A (4m) and B (4n). */
+typedef struct {
+  int m, n, k, N;
+  const double* A; long long lda;
+  const double* B; long long ldb;
+  double* C; long long ldc;
+  double alpha, beta;
+  const int32_t* C32; long long c_plane;
+  const int32_t* rs;
+  const int32_t* cs;
+} ggemm_recon_desc_t;
+
+#define GGEMM_STAGE_REPAIR_OFF 0
+#define GGEMM_STAGE_REPAIR_COUNT 1
+#define GGEMM_STAGE_REPAIR_ON 2
+
+/* Device scratch a stage call needs for num descriptors (caller-allocated, device memory). */
+size_t ggemm_stage_scratch_bytes(int num);
+/* Device counters: 4 x uint64 {nonfinite vectors, uncertified, repaired, safety fallback}
+ * followed by a uint32 status word (0 = ok); 64 bytes, caller-allocated and zeroed. */
+#define GGEMM_STAGE_COUNTER_BYTES 64
+
+/* Each enqueues exactly one kernel on `s` (none when there is no work).  Descriptors are
+ * HOST arrays; they are copied into `scratch` first.  Returns GGEMM_OK or GGEMM_ERR_*. */
+int ggemm_stage_prep(const ggemm_prep_desc_t* descs, int num, void* scratch,
+                     size_t scratch_bytes, void* counters, cudaStream_t s);
+int ggemm_stage_gemm(const ggemm_gemm_desc_t* descs, int num, void* scratch,
+                     size_t scratch_bytes, void* counters, cudaStream_t s);
+int ggemm_stage_recon(const ggemm_recon_desc_t* descs, int num, int repair_mode, void* scratch,
+                      size_t scratch_bytes, void* counters, cudaStream_t s);
+
+/* Host-only planner seam (replaces ggemm_plan, src/planner.cpp:281-330): plans num problems
+ * for the given path with an explicit device model, writing route / moduli / cost-model tile
+ * class per problem (route codes of the reference's ggemm_route_t, src/planner.h:7-17).
+ * rho_budget <= 0 uses GGEMM_RHO_BUDGET or 16.  Returns GGEMM_OK or GGEMM_ERR_*. */
+int ggemm_stage_plan(const ggemm_problem_t* problems, int num, const ggemm_config_t* cfg,
+                     int path, int num_sms, double fp64_flops, double int8_ops, double mem_bw,
+                     double tiny_mnk, double rho_budget, int* route, int* num_moduli,
+                     int* tile_cfg);
+/* Host-only operand-reuse seam (replaces build_operand_reuse, src/operand_reuse.cpp:47-141).
+ * nmod[g] <= 0 marks a problem as not emulated; policy 0 = EXACT_N, 1 = PROMOTE.
+ * out[0..2] = {unique A, unique B, promoted}, then 7 arrays of num ints: ua_rep, ua_nmod,
+ * ub_rep, ub_nmod (unused tails -1 / 0), prob_a, prob_b, eff_nmod. */
+int ggemm_stage_reuse(const ggemm_problem_t* problems, int num, const int* nmod, int policy,
+                      int* out);
+
+/* Number of CUDA devices this library can see (0 on a machine without a GPU). */
+int ggemm_device_count(void);
+/* Version string of this library. */
+const char* ggemm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
