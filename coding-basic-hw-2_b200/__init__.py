@@ -157,6 +157,10 @@ def _load():
                                      POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
         "ggemm_stage_reuse": (c_int, [POINTER(Problem), c_int, POINTER(c_int), c_int,
                                       POINTER(c_int)]),
+        "ggemm_set_stage_events": (c_int, [c_void_p, c_void_p]),
+        "ggemm_device_status": (c_int, [c_void_p]),
+        "ggemm_shard_group": (c_int, [POINTER(Problem), c_int, c_int, POINTER(Problem),
+                                      POINTER(c_int), POINTER(c_int), c_int, POINTER(c_int)]),
         "ggemm_device_count": (c_int, []),
         "ggemm_version": (c_char_p, []),
     }
@@ -233,6 +237,17 @@ class Handle:
                                      problems, int(num), ctypes.byref(st))
         return rc, st
 
+    def set_stage_events(self, events):
+        """events: 4 torch.cuda.Event (already recorded once, so the CUDA events exist) or
+        None to stop recording."""
+        if events is None:
+            return lib.ggemm_set_stage_events(self.ptr, None)
+        arr = (c_void_p * 4)(*[e.cuda_event for e in events])
+        return lib.ggemm_set_stage_events(self.ptr, arr)
+
+    def device_status(self):
+        return lib.ggemm_device_status(self.ptr)
+
     def close(self):
         if self.ptr:
             lib.ggemm_destroy(self.ptr)
@@ -249,6 +264,21 @@ class Handle:
             self.close()
         except Exception:
             pass
+
+
+def shard_group(problems, num, num_shards, out_cap=None):
+    """ggemm_shard_group: returns (sub-problem array, shard list, source-problem list)."""
+    cap = out_cap or max(16, 4 * num + 64 * num_shards)
+    out = (Problem * cap)()
+    sh = (c_int * cap)()
+    src = (c_int * cap)()
+    nout = c_int(0)
+    rc = lib.ggemm_shard_group(problems, int(num), int(num_shards), out, sh, src, cap,
+                               ctypes.byref(nout))
+    if rc != OK:
+        raise RuntimeError(f"ggemm_shard_group failed: {rc}")
+    n = nout.value
+    return out, [sh[i] for i in range(n)], [src[i] for i in range(n)]
 
 
 def version() -> str:

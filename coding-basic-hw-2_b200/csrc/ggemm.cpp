@@ -20,6 +20,7 @@
 #include <cstring>
 #include <new>
 
+#include "ggemm_ext.h"
 #include "ggemm_graph.h"
 #include "internal.hpp"
 
@@ -494,10 +495,13 @@ int enqueue_native(ggemm_handle_t h, const ggemm_problem_t* probs, const int* id
 }
 
 int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* probs,
-                     const char* db, int repair, bool per_plane, cudaStream_t s,
+                     const char* db, int repair, bool per_plane, bool record, cudaStream_t s,
                      int* launches) {
   (void)c;
+  record = record && h->stage_ev_on && h->chunks.size() == 1;
+  auto mark = [&](int i) { return !record || cudaEventRecord(h->stage_ev[i], s) == cudaSuccess; };
   for (const Chunk& ch : h->chunks) {
+    if (!mark(0)) return GGEMM_ERR_CUDA;
     if (ch.prep_blocks > 0) {
       if (launch_prep(reinterpret_cast<const ggemm_prep_desc_t*>(db + ch.off_prep),
                       reinterpret_cast<const int*>(db + ch.off_prep_prefix), ch.num_prep,
@@ -505,6 +509,7 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
         return GGEMM_ERR_NUMERICS;
       ++*launches;
     }
+    if (!mark(1)) return GGEMM_ERR_CUDA;
     const GemmJob* jobs = reinterpret_cast<const GemmJob*>(db + ch.off_jobs);
     const long long* jp = reinterpret_cast<const long long*>(db + ch.off_job_prefix);
     if (per_plane) {
@@ -521,6 +526,7 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
       if (launch_gemm(jobs, jp, ch.count, ch.tiles, h->counters, s)) return GGEMM_ERR_I8GEMM;
       ++*launches;
     }
+    if (!mark(2)) return GGEMM_ERR_CUDA;
     if (ch.recon_blocks > 0) {
       if (launch_recon(reinterpret_cast<const ggemm_recon_desc_t*>(db + ch.off_recon),
                        reinterpret_cast<const long long*>(db + ch.off_recon_prefix), ch.count,
@@ -528,6 +534,7 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
         return GGEMM_ERR_NUMERICS;
       ++*launches;
     }
+    if (!mark(3)) return GGEMM_ERR_CUDA;
   }
   return GGEMM_OK;
 }
@@ -614,7 +621,7 @@ static int path_emu(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* c
   if (c.blob_bytes)
     if (cudaMemcpyAsync(db, hb, c.blob_bytes, cudaMemcpyHostToDevice, h->stream) != cudaSuccess)
       return GGEMM_ERR_CUDA;
-  r = enqueue_emu_call(h, c, probs, db, repair, path == GGEMM_PATH_EMU_LOOP, h->stream,
+  r = enqueue_emu_call(h, c, probs, db, repair, path == GGEMM_PATH_EMU_LOOP, true, h->stream,
                        &st->kernel_launches);
   if (!r && c.nn > 0)
     r = enqueue_native(h, probs, h->nat.data(), c.nn, c.nn >= 2, c.nat_groups,
@@ -798,4 +805,29 @@ extern "C" int ggemm_grouped_dgemm(ggemm_handle_t h, ggemm_path_t path,
       return r;
     default: return GGEMM_ERR_INVALID;
   }
+}
+
+extern "C" int ggemm_set_stage_events(ggemm_handle_t h, cudaEvent_t* events) {
+  if (!h) return GGEMM_ERR_INVALID;
+  if (!events) {
+    h->stage_ev_on = false;
+    return GGEMM_OK;
+  }
+  for (int i = 0; i < 4; ++i) {
+    if (!events[i]) return GGEMM_ERR_INVALID;
+    h->stage_ev[i] = events[i];
+  }
+  h->stage_ev_on = true;
+  return GGEMM_OK;
+}
+
+extern "C" int ggemm_device_status(ggemm_handle_t h) {
+  if (!h) return -1;
+  DevCounters c{};
+  if (cudaSetDevice(h->device) != cudaSuccess ||
+      cudaMemcpyAsync(&c, h->counters, sizeof c, cudaMemcpyDeviceToHost, h->stream) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(h->stream) != cudaSuccess)
+    return -1;
+  return (int)c.status;
 }

@@ -82,7 +82,8 @@ static int enqueue(ggemm_plan_t p, cudaStream_t s, int* launches) {
   std::copy(p->nat.begin(), p->nat.end(), h->nat.begin());
   std::copy(p->plan.begin(), p->plan.end(), h->plan.begin());
   h->ngroups = p->ngroups;
-  int r = enqueue_emu_call(h, p->call, p->probs.data(), p->d_blob, p->repair, false, s, launches);
+  int r = enqueue_emu_call(h, p->call, p->probs.data(), p->d_blob, p->repair, false, false, s,
+                           launches);
   if (!r && p->call.nn > 0)
     r = enqueue_native(h, p->probs.data(), h->nat.data(), p->call.nn, p->call.nn >= 2,
                        p->call.nat_groups, p->d_blob + p->call.off_nat_ptrs, s, launches);

@@ -96,6 +96,8 @@ struct ggemm_handle_s {
   int reuse_promote = 0;
   int stats_repair = 0;
   int ws_diag_printed = 0;
+  cudaEvent_t stage_ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  bool stage_ev_on = false;
 };
 
 namespace g2 {
@@ -120,9 +122,9 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
                    const ggemm_problem_t* probs, int num, char* hb, const char* db,
                    EmuCall* out);
 // Enqueues the launches of a built call on s (descriptors already on the device at db).
-// per_plane: EMU_LOOP (one GEMM launch per plane).
+// per_plane: EMU_LOOP (one GEMM launch per plane).  record: stage events (ggemm_ext.h).
 int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* probs,
-                     const char* db, int repair, bool per_plane, cudaStream_t s,
+                     const char* db, int repair, bool per_plane, bool record, cudaStream_t s,
                      int* launches);
 int enqueue_native(ggemm_handle_t h, const ggemm_problem_t* probs, const int* idx, int cnt,
                    bool grouped, int ngroups, const char* d_ptrs, cudaStream_t s, int* launches);
