@@ -215,3 +215,15 @@ extern "C" int ggemm_stage_reuse(const ggemm_problem_t* problems, int num, const
   for (int i = 0; i < num; ++i) o[i] = r.eff_nmod[i];
   return GGEMM_OK;
 }
+
+extern "C" size_t ggemm_stage_crt_tables(void* out, size_t bytes) {
+  int st = 0;
+  const CrtTables& t = crt_tables(&st);
+  if (st != 0) return 0;
+  if (out) std::memcpy(out, &t, bytes < sizeof t ? bytes : sizeof t);
+  return sizeof t;
+}
+
+extern "C" double ggemm_stage_error_bound(int k, int num_moduli) {
+  return error_bound(k, num_moduli);
+}

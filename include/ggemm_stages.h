@@ -7,7 +7,8 @@
  *   ggemm_stage_prep    replaces oz2_prep_grouped          (src/ozaki2_numerics.cu:609-623)
  *   ggemm_stage_gemm    replaces i8_grouped_gemm / _launch (src/int8_grouped_gemm.cu:711-780)
  *   ggemm_stage_recon   replaces oz2_reconstruct_grouped   (src/ozaki2_numerics.cu:625-637)
- *   ggemm_stage_counters_* replace oz2_read_counters       (src/ozaki2_numerics.cu:675-693)
+ * Counters (oz2_read_counters, src/ozaki2_numerics.cu:675-693) are a caller-owned 64-byte
+ * device block, read back by the caller.
  *
  * Residue planes are stored in this library's own layout: each plane is the image of a K-major
  * tensor-core operand with 32-byte swizzle, so the GEMM fetches a tile with one bulk copy per
@@ -117,6 +118,13 @@ int ggemm_stage_plan(const ggemm_problem_t* problems, int num, const ggemm_confi
  * ub_rep, ub_nmod (unused tails -1 / 0), prob_a, prob_b, eff_nmod. */
 int ggemm_stage_reuse(const ggemm_problem_t* problems, int num, const int* nmod, int policy,
                       int* out);
+
+/* Host-only: copies the CRT constant tables (same content and layout as the reference's
+ * oz2_crt_tables, src/moduli.h:43-58) into out (up to `bytes`); returns their size, 0 on a
+ * table-construction failure.  ggemm_stage_error_bound is the a-priori bound of
+ * src/ozaki2_numerics.cu:639-650. */
+size_t ggemm_stage_crt_tables(void* out, size_t bytes);
+double ggemm_stage_error_bound(int k, int num_moduli);
 
 /* Number of CUDA devices this library can see (0 on a machine without a GPU). */
 int ggemm_device_count(void);
