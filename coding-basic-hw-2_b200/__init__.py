@@ -163,6 +163,7 @@ def _load():
                                       POINTER(c_int), POINTER(c_int), c_int, POINTER(c_int)]),
         "ggemm_stage_crt_tables": (c_size_t, [c_void_p, c_size_t]),
         "ggemm_stage_error_bound": (c_double, [c_int, c_int]),
+        "ggemm_dgemm_noalloc": (c_int, [POINTER(Problem), c_int, c_int, c_void_p]),
         "ggemm_device_count": (c_int, []),
         "ggemm_version": (c_char_p, []),
     }

@@ -41,6 +41,27 @@ int ggemm_shard_group(const ggemm_problem_t* problems, int num, int num_shards,
                       ggemm_problem_t* out, int* out_shard, int* out_src, int out_cap,
                       int* num_out);
 
+/* One emulated FP64 GEMM, C = alpha*A*B + beta*C (column-major, device pointers on the current
+ * device), for callers that cannot allocate device memory: code that owns no CUDA allocator,
+ * runs inside another runtime's memory pool, or must not call cudaMalloc / cudaFree.  It has
+ * no counterpart in the reference.  The caller passes inputs and outputs; all scratch (residue
+ * images, int32 products, workspace, descriptors, counters) lives in one fixed 64 MiB device
+ * array compiled into this library, which every GPU that loads the library holds until exit.
+ * Nothing is allocated: no cudaMalloc / cudaFree, no allocating library routine.
+ *   num_moduli: 0 = adaptive (target 1e-15) or a fixed N in [2, 20];
+ *   repair_mode: GGEMM_REPAIR_* (default = COUNT, as GGEMM_PATH_EMU_GROUPED).
+ * Results equal ggemm_grouped_dgemm(GGEMM_PATH_EMU_GROUPED) of the same problem, bit for bit.
+ * A problem whose scratch exceeds 64 MiB (about 830^3 at N = 15) returns GGEMM_ERR_WORKSPACE
+ * with a one-line message on stderr, before anything is enqueued; k > 131040 returns
+ * GGEMM_ERR_UNSAFE.
+ * The first call on a device does a one-time set-up with that device current (uploads the CRT
+ * constants, which synchronizes the device, and looks up the array's device address); make that
+ * first call before any stream capture.  Work is enqueued on `stream`.  Every call shares the
+ * array and finds the previous call's contents in it: calls that overlap on the GPU (other
+ * streams, other host threads) race and must be ordered by the caller. */
+int ggemm_dgemm_noalloc(const ggemm_problem_t* problem, int num_moduli, int repair_mode,
+                        cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
