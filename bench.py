@@ -305,7 +305,7 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
 
     # global group, then this rank's shard
-    gshapes = c2_shapes(PROBS_PER_GPU * world)
+    gshapes = c2_shapes(args.problems * world)
     if world > 1:
         logical = g2.make_problems([dict(m=m, n=n, k=k, A=0x1000 * (i + 1), lda=m,
                                          B=0x100000000 * (i + 1), ldb=k,
@@ -389,6 +389,18 @@ def run_ours(args):
     t_max = max_over_ranks(elapsed)
     flops_all = total_over_ranks(grp.flops)
     value = flops_all * args.steps / t_max / 1e12
+
+    if args.quick:
+        if rank == 0:
+            print(json.dumps({"quick": True, "value": value, "unit": "TFLOP/s",
+                              "ms_per_step": t_max / args.steps * 1e3,
+                              "stage_ms": [float(x) for x in stage_ms],
+                              "problems_per_gpu": grp.num, "moduli": nmod}), flush=True)
+        handle.close()
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
 
     # ------------------------------------------------------------------- end-to-end timing
     hA = torch.empty(grp.A.shape, dtype=torch.float64, pin_memory=True)
@@ -524,6 +536,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--problems", type=int, default=PROBS_PER_GPU,
+                    help="problems per GPU (64 = the C2 workload; fewer for profiling)")
+    ap.add_argument("--quick", action="store_true",
+                    help="device-resident timing only (profiling runs): no e2e, cuBLAS, "
+                         "certified or CPU legs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -238,9 +238,9 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       const ggemm_problem_t& p = probs[g];
       const int N = plan[g].num_moduli;
       const int ua = h->ua_of[j], ub = h->ub_of[j];
-      const int cid = (int)h->chunks.size();
       const bool chunk_per_problem = loop || lbat;
       for (int attempt = 0; attempt < 2; ++attempt) {
+        const int cid = (int)h->chunks.size();  // id of the open chunk (changes on a retry)
         const bool new_a = h->ua_chunk[ua] != cid;
         const bool new_b = h->ub_chunk[ub] != cid;
         const size_t na = new_a ? img_bytes(p.m, p.k, h->ua_n[ua]) : 0;

@@ -129,16 +129,17 @@ __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, ui
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// Residue words of 4 elements for planes 0..N-1 into out[l].
+// Residue words of 4 elements for planes 1..N-1, each stored as soon as it is packed
+// (word l goes to dst + l * pb) so that no per-plane array stays live in registers.
 template <int D>
-__device__ __forceinline__ void residue_words4(const ElemDigits (&e)[4], int N,
-                                               uint32_t (&out)[kMaxModuli]) {
-  out[0] = pack4(e[0].low, e[1].low, e[2].low, e[3].low);
+__device__ __forceinline__ void store_odd_planes4(const ElemDigits (&e)[4], int N, int8_t* dst,
+                                                  long long pb, bool store) {
 #pragma unroll
   for (int l = 1; l < kMaxModuli; ++l) {
     if (l >= N) break;
-    out[l] = pack4(odd_residue_byte<D>(e[0], l), odd_residue_byte<D>(e[1], l),
-                   odd_residue_byte<D>(e[2], l), odd_residue_byte<D>(e[3], l));
+    const uint32_t w = pack4(odd_residue_byte<D>(e[0], l), odd_residue_byte<D>(e[1], l),
+                             odd_residue_byte<D>(e[2], l), odd_residue_byte<D>(e[3], l));
+    if (store) *reinterpret_cast<uint32_t*>(dst + l * pb) = w;
   }
 }
 
@@ -234,11 +235,11 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
   const long long pb = d.plane_bytes;
 
   double da = 0.0, na = 0.0;  // chain t = w
-  for (int k0 = 0; k0 < ksteps * 32; k0 += 64) {
+  for (int k0 = 0; k0 < ksteps * 32; k0 += 32) {
     // ||dA||^2, ||A'||^2 chains: q = k0 + w + 8 j (the reference's chain order)
     if (sh != kShiftNonfinite) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         const int q = k0 + w + 8 * j;
         const double a = (valid && q < K) ? X[r + q * ld] : 0.0;
         const double xs = mul_pow2(a, sh);
@@ -248,42 +249,24 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
         na = fma(xt, xt, na);
       }
     }
-    // residues of 8 consecutive K positions q0 .. q0+7 (8 bytes per plane)
-    const int q0 = k0 + 8 * w;
-    const bool store = in_image && (q0 >> 5) < ksteps;
-    ElemDigits e[2][4];
-    uint32_t absw[2];
+    // residues of the 4 consecutive K positions q0 .. q0+3 (4 bytes per plane)
+    const int q0 = k0 + 4 * w;
+    ElemDigits e[4];
+    uint32_t ab[4];
     bool wide = false;
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      uint32_t ab[4];
-#pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        const int q = q0 + 4 * g + x;
-        const double a = (valid && q < K) ? X[r + q * ld] : 0.0;
-        split_digits(scaled_trunc(a, sh), e[g][x]);
-        ab[x] = (sh == kShiftNonfinite) ? 0u : abs_byte(a, sg);
-        wide |= e[g][x].wide;
-      }
-      absw[g] = pack4(ab[0], ab[1], ab[2], ab[3]);
+    for (int x = 0; x < 4; ++x) {
+      const int q = q0 + x;
+      const double a = (valid && q < K) ? X[r + q * ld] : 0.0;
+      split_digits(scaled_trunc(a, sh), e[x]);
+      ab[x] = (sh == kShiftNonfinite) ? 0u : abs_byte(a, sg);
+      wide |= e[x].wide;
     }
-    uint32_t w0[kMaxModuli], w1[kMaxModuli];
-    if (__any_sync(0xFFFFFFFFu, wide)) {
-      residue_words4<8>(e[0], N, w0);
-      residue_words4<8>(e[1], N, w1);
-    } else {
-      residue_words4<6>(e[0], N, w0);
-      residue_words4<6>(e[1], N, w1);
-    }
-    if (store) {
-      int8_t* dst = d.img + img_off(rg, r, q0);
-#pragma unroll
-      for (int l = 0; l < kMaxModuli; ++l) {
-        if (l >= N) break;
-        *reinterpret_cast<uint2*>(dst + l * pb) = make_uint2(w0[l], w1[l]);
-      }
-      *reinterpret_cast<uint2*>(dst + N * pb) = make_uint2(absw[0], absw[1]);
-    }
+    int8_t* dst = d.img + img_off(rg, r, q0);
+    if (in_image) *reinterpret_cast<uint32_t*>(dst) = pack4(e[0].low, e[1].low, e[2].low, e[3].low);
+    if (__any_sync(0xFFFFFFFFu, wide)) store_odd_planes4<8>(e, N, dst, pb, in_image);
+    else store_odd_planes4<6>(e, N, dst, pb, in_image);
+    if (in_image) *reinterpret_cast<uint32_t*>(dst + N * pb) = pack4(ab[0], ab[1], ab[2], ab[3]);
   }
   __syncthreads();
   sm.a[w][lane] = da;
@@ -367,20 +350,11 @@ __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters
       ab[x] = (sh == kShiftNonfinite) ? 0u : abs_byte(a, sg);
       wide |= e[x].wide;
     }
-    uint32_t wd[kMaxModuli];
-    if (__any_sync(0xFFFFFFFFu, wide))
-      residue_words4<8>(e, N, wd);
-    else
-      residue_words4<6>(e, N, wd);
-    if (in_k) {
-      int8_t* dst = d.img + img_off(rg, col, q0);
-#pragma unroll
-      for (int l = 0; l < kMaxModuli; ++l) {
-        if (l >= N) break;
-        *reinterpret_cast<uint32_t*>(dst + l * pb) = wd[l];
-      }
-      *reinterpret_cast<uint32_t*>(dst + N * pb) = pack4(ab[0], ab[1], ab[2], ab[3]);
-    }
+    int8_t* dst = d.img + img_off(rg, col, in_k ? q0 : 0);
+    if (in_k) *reinterpret_cast<uint32_t*>(dst) = pack4(e[0].low, e[1].low, e[2].low, e[3].low);
+    if (__any_sync(0xFFFFFFFFu, wide)) store_odd_planes4<8>(e, N, dst, pb, in_k);
+    else store_odd_planes4<6>(e, N, dst, pb, in_k);
+    if (in_k) *reinterpret_cast<uint32_t*>(dst + N * pb) = pack4(ab[0], ab[1], ab[2], ab[3]);
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
@@ -404,7 +378,7 @@ __device__ __forceinline__ int find_owner(const P* __restrict__ prefix, int num,
   return lo;
 }
 
-__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const ggemm_prep_desc_t* __restrict__ descs,
+__global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const ggemm_prep_desc_t* __restrict__ descs,
                                                             const int* __restrict__ prefix,
                                                             int num, DevCounters* cnt) {
   __shared__ PrepShared sm;
@@ -650,38 +624,34 @@ __device__ __forceinline__ double fp64_dot(const ggemm_recon_desc_t& d, int i, i
   return s;
 }
 
-// One output entry (src/ozaki2_numerics.cu:485-563): returns the value and bumps the counters.
-__device__ __forceinline__ void recon_entry(const ggemm_recon_desc_t& d, int mode, long long idx,
-                                            int i, int j, unsigned& n_unc, unsigned& n_rep,
-                                            unsigned& n_saf) {
-  const int N = d.N;
-  double* cp = d.C + i + (long long)j * d.ldc;
-  const double alpha = d.alpha, beta = d.beta;
-  const double c0 = (beta == 0.0) ? 0.0 : *cp;
-  if (alpha == 0.0) {
-    *cp = (beta == 0.0) ? 0.0 : beta * c0;
-    return;
-  }
-  const int rsh = d.rs[i], csh = d.cs[j];
-  if (rsh == kShiftNonfinite || csh == kShiftNonfinite) {
-    const double v = fp64_dot(d, i, j);
-    *cp = (beta == 0.0) ? alpha * v : fma(alpha, v, beta * c0);
-    ++n_saf;
-    return;
-  }
-  const int sig = d.rs[d.m + i], tau = d.cs[d.n + j];
-  if (sig == kShiftZero || tau == kShiftZero) {
-    *cp = (beta == 0.0) ? alpha * 0.0 : fma(alpha, 0.0, beta * c0);
-    return;
-  }
-  const int32_t* __restrict__ C32 = d.C32 + idx;
-  const long long cst = d.c_plane;
-  uint64_t S1 = 0;
-  uint32_t S2 = 0;
-#pragma unroll 4
-  for (int l = 0; l < N; ++l) {
+// Per-problem constants of the reconstruct (hoisted out of the entry loop).
+struct ReconCtx {
+  double gam, crt_u, inv_u1;
+  int N, lu1;
+};
+
+__device__ __forceinline__ ReconCtx recon_ctx(const ggemm_recon_desc_t& d) {
+  ReconCtx cx;
+  const double u = 0x1p-53;
+  const double nt = (double)d.k + (d.alpha != 1.0 ? 1.0 : 0.0) + (d.beta != 0.0 ? 1.0 : 0.0);
+  cx.gam = (nt * u / fma(-nt, u, 1.0) - 2.0 * u) * (1.0 - 0x1p-40);
+  cx.N = d.N;
+  cx.lu1 = c_tab.log2_u1[d.N];
+  cx.crt_u = d.N * 255.0 * 0x1p-19 + 0x1p-10;
+  cx.inv_u1 = __longlong_as_double((long long)(1023 - cx.lu1) << 52);
+  return cx;
+}
+
+// S1 = sum s1_l y_l, S2 = sum s2_l y_l with y_l = (c_l mod p_l) q_l mod p_l (exact integers).
+__device__ __forceinline__ void crt_sums(const int32_t (&v)[kMaxModuli + 1], int N, uint64_t& S1,
+                                         uint32_t& S2) {
+  S1 = 0;
+  S2 = 0;
+#pragma unroll
+  for (int l = 0; l < kMaxModuli; ++l) {
+    if (l >= N) break;
     const uint32_t p = c_tab.p[l], mg = c_tab.magic[l];
-    const int32_t c = __ldg(C32 + l * cst);
+    const int32_t c = v[l];
     const uint32_t uc = c < 0 ? 0u - (uint32_t)c : (uint32_t)c;
     uint32_t r = mod_p(uc, p, mg);
     if (c < 0 && r) r = p - r;
@@ -689,37 +659,40 @@ __device__ __forceinline__ void recon_entry(const ggemm_recon_desc_t& d, int mod
     S1 += c_tab.s1[N][l] * (uint64_t)y;
     S2 += c_tab.s2[N][l] * y;
   }
+}
+
+// Everything after the CRT sums for one entry (src/ozaki2_numerics.cu:519-563).
+__device__ __forceinline__ void recon_finish(const ggemm_recon_desc_t& d, const ReconCtx& cx,
+                                             int mode, int i, int j, double* cp, double c0,
+                                             uint64_t S1, uint32_t S2, int32_t L32, int rsh,
+                                             int csh, int sig, int tau, float fda, float fna,
+                                             float fdb, float fnb, unsigned& n_unc,
+                                             unsigned& n_rep) {
+  const double alpha = d.alpha, beta = d.beta;
+  const int N = cx.N;
   const double s2d = (double)S2 * 0x1p-18;
   const double Q = rint(((double)S1 + s2d) * c_tab.inv_Pu[N]);
   const long long X1 = (long long)S1 - (long long)Q * c_tab.P1[N];
   const double xr = (double)X1 + fma(-Q, c_tab.P2[N], s2d);
-  const int lu1 = c_tab.log2_u1[N];
-  const int esc = lu1 - rsh - csh;
+  const int esc = cx.lu1 - rsh - csh;
   const double v = mul_pow2(xr, esc);
   const double emu = (beta == 0.0) ? alpha * v : fma(alpha, v, beta * c0);
   if (mode == GGEMM_STAGE_REPAIR_OFF || (beta != 0.0 && !isfinite(c0))) {
     *cp = emu;
     return;
   }
-  // certificate: rigorous error bound E vs gamma_n (|alpha| lower(|A||B|) + |beta C0|)
   const double u = 0x1p-53;
-  const double nt = (double)d.k + (alpha != 1.0 ? 1.0 : 0.0) + (beta != 0.0 ? 1.0 : 0.0);
-  const double gam = (nt * u / fma(-nt, u, 1.0) - 2.0 * u) * (1.0 - 0x1p-40);
-  const double crt_u = N * 255.0 * 0x1p-19 + 0x1p-10;
-  const double da = __int_as_float(d.rs[2 * d.m + i]), na = __int_as_float(d.rs[3 * d.m + i]);
-  const double db = __int_as_float(d.cs[2 * d.n + j]), nb = __int_as_float(d.cs[3 * d.n + j]);
+  const double da = fda, na = fna, db = fdb, nb = fnb;
   const double et = fma(da, nb, fma(na, db, da * db)) * (1.0 + 0x1p-40);
-  const double inv_u1 = __longlong_as_double((long long)(1023 - lu1) << 52);
-  const double Eu = fma(4.0 * u, fabs(xr), fma(et, inv_u1, crt_u)) * (1.0 + 0x1p-40);
+  const double Eu = fma(4.0 * u, fabs(xr), fma(et, cx.inv_u1, cx.crt_u)) * (1.0 + 0x1p-40);
   const double E = mul_pow2(Eu, esc);
-  const double L = (double)__ldg(C32 + N * cst);
-  double lab = mul_pow2(L, -(sig + tau));
+  double lab = mul_pow2((double)L32, -(sig + tau));
   lab = fmax(lab, fabs(v) - E) * (1.0 - 0x1p-40);
   if (lab < 0x1p-1000) lab = 0.0;
   const double aalpha = fabs(alpha);
   const double lhs = aalpha * E * (1.0 + 0x1p-40);
-  const double rhs = gam * fma(aalpha, lab, fabs(beta * c0)) * (1.0 - 0x1p-40);
-  const bool cert = gam > 0.0 && E >= 0x1p-1000 && isfinite(lhs) && isfinite(v) && lhs <= rhs;
+  const double rhs = cx.gam * fma(aalpha, lab, fabs(beta * c0)) * (1.0 - 0x1p-40);
+  const bool cert = cx.gam > 0.0 && E >= 0x1p-1000 && isfinite(lhs) && isfinite(v) && lhs <= rhs;
   if (cert) {
     *cp = emu;
   } else if (mode == GGEMM_STAGE_REPAIR_COUNT) {
@@ -732,7 +705,108 @@ __device__ __forceinline__ void recon_entry(const ggemm_recon_desc_t& d, int mod
   }
 }
 
-__global__ void __launch_bounds__(kReconThreads) recon_kernel(const ggemm_recon_desc_t* __restrict__ descs,
+// The cases that never read the int32 products (src/ozaki2_numerics.cu:492-504).  Returns true
+// when the entry is done.
+__device__ __forceinline__ bool recon_special(const ggemm_recon_desc_t& d, int i, int j,
+                                              double* cp, double c0, int rsh, int csh, int sig,
+                                              int tau, unsigned& n_saf) {
+  const double alpha = d.alpha, beta = d.beta;
+  if (alpha == 0.0) {
+    *cp = (beta == 0.0) ? 0.0 : beta * c0;
+    return true;
+  }
+  if (rsh == kShiftNonfinite || csh == kShiftNonfinite) {
+    const double v = fp64_dot(d, i, j);
+    *cp = (beta == 0.0) ? alpha * v : fma(alpha, v, beta * c0);
+    ++n_saf;
+    return true;
+  }
+  if (sig == kShiftZero || tau == kShiftZero) {
+    *cp = (beta == 0.0) ? alpha * 0.0 : fma(alpha, 0.0, beta * c0);
+    return true;
+  }
+  return false;
+}
+
+// One entry, scalar loads (any m).
+__device__ __forceinline__ void recon_entry(const ggemm_recon_desc_t& d, const ReconCtx& cx,
+                                            int mode, long long idx, int i, int j,
+                                            unsigned& n_unc, unsigned& n_rep, unsigned& n_saf) {
+  double* cp = d.C + i + (long long)j * d.ldc;
+  const double c0 = (d.beta == 0.0) ? 0.0 : *cp;
+  const int rsh = d.alpha == 0.0 ? 0 : d.rs[i], csh = d.alpha == 0.0 ? 0 : d.cs[j];
+  const int sig = d.alpha == 0.0 ? 0 : d.rs[d.m + i], tau = d.alpha == 0.0 ? 0 : d.cs[d.n + j];
+  if (recon_special(d, i, j, cp, c0, rsh, csh, sig, tau, n_saf)) return;
+  int32_t v[kMaxModuli + 1];
+  const int32_t* __restrict__ C32 = d.C32 + idx;
+#pragma unroll
+  for (int l = 0; l <= kMaxModuli; ++l)
+    if (l <= cx.N) v[l] = __ldg(C32 + l * d.c_plane);
+  uint64_t S1;
+  uint32_t S2;
+  crt_sums(v, cx.N, S1, S2);
+  int32_t L = 0;
+#pragma unroll
+  for (int l = 0; l <= kMaxModuli; ++l)
+    if (l == cx.N) L = v[l];
+  recon_finish(d, cx, mode, i, j, cp, c0, S1, S2, L, rsh, csh, sig, tau,
+               __int_as_float(d.rs[2 * d.m + i]), __int_as_float(d.rs[3 * d.m + i]),
+               __int_as_float(d.cs[2 * d.n + j]), __int_as_float(d.cs[3 * d.n + j]), n_unc, n_rep);
+}
+
+// Two consecutive rows i0, i0+1 of column j with 8-byte loads of every plane (m even): all
+// N+1 loads are issued before any arithmetic, so each thread keeps (N+1) x 8 bytes in flight.
+__device__ __forceinline__ void recon_pair(const ggemm_recon_desc_t& d, const ReconCtx& cx,
+                                           int mode, long long e0, int i0, int j,
+                                           unsigned& n_unc, unsigned& n_rep, unsigned& n_saf) {
+  const int N = cx.N;
+  int2 c2[kMaxModuli + 1];
+  const int2* __restrict__ src = reinterpret_cast<const int2*>(d.C32 + e0);
+  const long long pst = d.c_plane >> 1;
+  const bool need_planes = d.alpha != 0.0;
+  if (need_planes) {
+#pragma unroll
+    for (int l = 0; l <= kMaxModuli; ++l)
+      if (l <= N) c2[l] = __ldg(src + l * pst);
+  }
+  const double beta = d.beta;
+  double* cbase = d.C + i0 + (long long)j * d.ldc;
+  int2 rsh2 = make_int2(0, 0), sig2 = rsh2, da2 = rsh2, na2 = rsh2;
+  int csh = 0, tau = 0;
+  float fdb = 0.f, fnb = 0.f;
+  if (need_planes) {
+    rsh2 = __ldg(reinterpret_cast<const int2*>(d.rs + i0));
+    sig2 = __ldg(reinterpret_cast<const int2*>(d.rs + d.m + i0));
+    da2 = __ldg(reinterpret_cast<const int2*>(d.rs + 2 * d.m + i0));
+    na2 = __ldg(reinterpret_cast<const int2*>(d.rs + 3 * d.m + i0));
+    csh = __ldg(d.cs + j);
+    tau = __ldg(d.cs + d.n + j);
+    fdb = __int_as_float(__ldg(d.cs + 2 * d.n + j));
+    fnb = __int_as_float(__ldg(d.cs + 3 * d.n + j));
+  }
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    double* cp = cbase + x;
+    const double c0 = (beta == 0.0) ? 0.0 : *cp;
+    const int rsh = x ? rsh2.y : rsh2.x, sig = x ? sig2.y : sig2.x;
+    if (recon_special(d, i0 + x, j, cp, c0, rsh, csh, sig, tau, n_saf)) continue;
+    int32_t v[kMaxModuli + 1];
+#pragma unroll
+    for (int l = 0; l <= kMaxModuli; ++l) v[l] = x ? c2[l].y : c2[l].x;
+    uint64_t S1;
+    uint32_t S2;
+    crt_sums(v, N, S1, S2);
+    int32_t L = 0;
+#pragma unroll
+    for (int l = 0; l <= kMaxModuli; ++l)
+      if (l == N) L = v[l];
+    recon_finish(d, cx, mode, i0 + x, j, cp, c0, S1, S2, L, rsh, csh, sig, tau,
+                 __int_as_float(x ? da2.y : da2.x), __int_as_float(x ? na2.y : na2.x), fdb, fnb,
+                 n_unc, n_rep);
+  }
+}
+
+__global__ void __launch_bounds__(kReconThreads, 2) recon_kernel(const ggemm_recon_desc_t* __restrict__ descs,
                                                               const long long* __restrict__ prefix,
                                                               int num, int mode,
                                                               DevCounters* cnt) {
@@ -740,15 +814,29 @@ __global__ void __launch_bounds__(kReconThreads) recon_kernel(const ggemm_recon_
   const ggemm_recon_desc_t d = descs[owner];
   unsigned n_unc = 0, n_rep = 0, n_saf = 0;
   if (d.N >= 1 && d.N <= kMaxModuli && d.m > 0 && d.n > 0) {
+    const ReconCtx cx = recon_ctx(d);
     const long long mn = (long long)d.m * d.n;
-    const long long base = ((long long)blockIdx.x - prefix[owner]) * (kReconThreads * kReconPerThread);
+    const long long base =
+        ((long long)blockIdx.x - prefix[owner]) * (kReconThreads * kReconPerThread);
+    const bool vec = (d.m & 1) == 0 && (d.c_plane & 1) == 0 &&
+                     ((uintptr_t)d.C32 & 7) == 0 && ((uintptr_t)d.rs & 7) == 0;
+    if (vec) {
 #pragma unroll 1
-    for (int e = 0; e < kReconPerThread; ++e) {
-      const long long idx = base + e * kReconThreads + threadIdx.x;
-      if (idx >= mn) break;
-      const int j = (int)(idx / d.m);
-      const int i = (int)(idx - (long long)j * d.m);
-      recon_entry(d, mode, idx, i, j, n_unc, n_rep, n_saf);
+      for (int e = 0; e < kReconPerThread / 2; ++e) {
+        const long long e0 = base + 2 * ((long long)e * kReconThreads + threadIdx.x);
+        if (e0 >= mn) break;
+        const int j = (int)(e0 / d.m);
+        recon_pair(d, cx, mode, e0, (int)(e0 - (long long)j * d.m), j, n_unc, n_rep, n_saf);
+      }
+    } else {
+#pragma unroll 1
+      for (int e = 0; e < kReconPerThread; ++e) {
+        const long long idx = base + e * kReconThreads + threadIdx.x;
+        if (idx >= mn) break;
+        const int j = (int)(idx / d.m);
+        const int i = (int)(idx - (long long)j * d.m);
+        recon_entry(d, cx, mode, idx, i, j, n_unc, n_rep, n_saf);
+      }
     }
   }
   // counters: warp reduce, block reduce, at most one atomic per counter per block
