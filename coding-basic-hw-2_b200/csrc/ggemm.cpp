@@ -363,9 +363,9 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       std::sort(order, order + ch.count, [&](int a, int b) {
         const ggemm_problem_t &pa = probs[emu[a]], &pb = probs[emu[b]];
         if (pa.k != pb.k) return pa.k > pb.k;
-        const long long ta = (long long)((pa.m + 127) / 128) * ((pa.n + 127) / 128) *
+        const long long ta = (long long)((pa.m + 127) / 128) * ((pa.n + 255) / 256) *
                              (plan[emu[a]].num_moduli + 1);
-        const long long tb = (long long)((pb.m + 127) / 128) * ((pb.n + 127) / 128) *
+        const long long tb = (long long)((pb.m + 127) / 128) * ((pb.n + 255) / 256) *
                              (plan[emu[b]].num_moduli + 1);
         if (ta != tb) return ta > tb;
         return a < b;
@@ -388,10 +388,7 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       base.m = p.m;
       base.n = p.n;
       base.ksteps = (p.k + 31) / 32;
-      base.rga = (p.m + 7) / 8;
-      base.rgb = (p.n + 7) / 8;
-      base.tm = (p.m + kGemmBM - 1) / kGemmBM;
-      base.tn = (p.n + kGemmBN - 1) / kGemmBN;
+      set_gemm_tiling(base);
       if (loop) {
         for (int l = 0; l <= N; ++l) {
           GemmJob jb = base;
@@ -516,8 +513,11 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
       // EMU_LOOP: one problem per chunk, one GEMM launch per plane (own 2-entry prefix)
       const ggemm_problem_t& p = probs[h->emu[ch.first]];
       const int planes = h->plan[h->emu[ch.first]].num_moduli + 1;
-      const long long tiles =
-          (long long)((p.m + kGemmBM - 1) / kGemmBM) * ((p.n + kGemmBN - 1) / kGemmBN);
+      GemmJob shape{};
+      shape.m = p.m;
+      shape.n = p.n;
+      set_gemm_tiling(shape);
+      const long long tiles = (long long)shape.tm * shape.tn;
       for (int q = 0; q < planes && tiles > 0; ++q) {
         if (launch_gemm(jobs + q, jp + 2 * q, 1, tiles, h->counters, s)) return GGEMM_ERR_I8GEMM;
         ++*launches;

@@ -391,16 +391,19 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const ggemm_prep_
 }
 
 // ============================================================================== GEMM kernel
-// Tile 128 x 128 x (4 x 32-byte K steps) per pipeline stage.  Warp roles:
-//   warp 0: TMEM allocation + bulk-copy producer (one lane)
+// Tile 128 x 256 (128 x 128 for n <= 128) x (4 x 32-byte K steps) per pipeline stage.
+// Warp roles:
+//   warp 0: TMEM allocation + bulk-copy producer (lanes 0-3 copy A, 4-7 copy B)
 //   warp 1: tcgen05.mma issuer (one lane)
 //   warps 2..5: epilogue (TMEM -> registers -> int32 stores); warp w reads TMEM lanes
 //   32 (w % 4) .. 32 (w % 4) + 31, i.e. tile rows.
-// Two TMEM accumulators (2 x 128 columns) let the epilogue of one tile overlap the MMAs of the
-// next.  Tiles are handed out statically (tile t to CTA t mod grid) from a host-side LPT order.
-constexpr int kStages = 6;
-constexpr int kStepBytes = 16 * 256;            // one 32-byte K step of 128 rows
-constexpr int kStageBytes = 2 * 4 * kStepBytes;  // A + B, 4 K steps each
+// Two TMEM accumulators (2 x 256 columns, all of TMEM) let the epilogue of one tile overlap the
+// MMAs of the next.  The 256-column tile halves the operand bytes fetched per MAC of the
+// B side, which (with 128 x 128 tiles) bound the kernel by L2 -> SM traffic.  Tiles are handed out statically (tile t to CTA t mod grid) from a host-side LPT order.
+constexpr int kStages = 4;
+constexpr int kStepBytesA = 16 * 256;                     // one 32-byte K step of 128 rows
+constexpr int kStepBytesB = 32 * 256;                     // ... of 256 rows
+constexpr int kStageBytes = 4 * (kStepBytesA + kStepBytesB);  // 4 K steps of A and B
 constexpr int kGemmThreads = 192;
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
 
@@ -463,7 +466,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(&ctl->tmem_base, 256);
+    tmem_alloc(&ctl->tmem_base, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -472,51 +475,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = ctl->tmem_base;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------- producer
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t armed = 0, last_par = 0;  // per stage: ever armed / parity of the last arming
-      for (long long t = blockIdx.x; t < total_tiles && !ctl->abort; t += gridDim.x) {
-        const TileInfo ti = decode_tile(jobs, prefix, num, t);
-        const GemmJob& jb = *ti.job;
-        const int g0a = ti.tm * 16, ga = min(16, jb.rga - g0a);
-        const int g0b = ti.tn * 16, gb = min(16, jb.rgb - g0b);
-        const int8_t* A = jb.A + (long long)ti.plane * jb.a_plane + (long long)g0a * 256;
-        const int8_t* B = jb.B + (long long)ti.plane * jb.b_plane + (long long)g0b * 256;
-        const long long astep = (long long)jb.rga * 256, bstep = (long long)jb.rgb * 256;
-        for (int ks = 0; ks < jb.ksteps; ks += 4) {
-          const int nst = min(4, jb.ksteps - ks);
-          if (!bounded_wait(&ctl->empty[stage], phase ^ 1u, ctl, cnt)) break;
-          mbar_arrive_expect_tx(&ctl->full[stage], (uint32_t)(nst * (ga + gb) * 256));
-          armed |= 1u << stage;
-          last_par = (last_par & ~(1u << stage)) | (phase << stage);
-          uint8_t* sa = smem + stage * kStageBytes;
-          uint8_t* sb = sa + 4 * kStepBytes;
-          for (int j = 0; j < nst; ++j) {
-            bulk_g2s(sa + j * kStepBytes, A + (long long)(ks + j) * astep, (uint32_t)(ga * 256),
-                     &ctl->full[stage]);
-            bulk_g2s(sb + j * kStepBytes, B + (long long)(ks + j) * bstep, (uint32_t)(gb * 256),
-                     &ctl->full[stage]);
-          }
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
+    // --------------------------------------------------------------------- producer
+    // Lane 0 waits for a free stage and arms its barrier; lanes 0-3 then copy the 4 K steps of
+    // A and lanes 4-7 those of B (parallel issue of the bulk copies).
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t armed = 0, last_par = 0;  // per stage: ever armed / parity of the last arming
+    for (long long t = blockIdx.x; t < total_tiles && !ctl->abort; t += gridDim.x) {
+      const TileInfo ti = decode_tile(jobs, prefix, num, t);
+      const GemmJob& jb = *ti.job;
+      const int g0a = ti.tm * 16, ga = min(16, jb.rga - g0a);
+      const int gbt = jb.bn / 8;
+      const int g0b = ti.tn * gbt, gb = min(gbt, jb.rgb - g0b);
+      const int8_t* A = jb.A + (long long)ti.plane * jb.a_plane + (long long)g0a * 256;
+      const int8_t* B = jb.B + (long long)ti.plane * jb.b_plane + (long long)g0b * 256;
+      const long long astep = (long long)jb.rga * 256, bstep = (long long)jb.rgb * 256;
+      bool ok = true;
+      for (int ks = 0; ks < jb.ksteps; ks += 4) {
+        const int nst = min(4, jb.ksteps - ks);
+        if (lane == 0) {
+          ok = bounded_wait(&ctl->empty[stage], phase ^ 1u, ctl, cnt);
+          if (ok) mbar_arrive_expect_tx(&ctl->full[stage], (uint32_t)(nst * (ga + gb) * 256));
+        }
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+        if (!ok) break;
+        armed |= 1u << stage;
+        last_par = (last_par & ~(1u << stage)) | (phase << stage);
+        uint8_t* sa = smem + stage * kStageBytes;
+        uint8_t* sb = sa + 4 * kStepBytesA;
+        if (lane < nst)
+          bulk_g2s(sa + lane * kStepBytesA, A + (long long)(ks + lane) * astep,
+                   (uint32_t)(ga * 256), &ctl->full[stage]);
+        else if (lane >= 4 && lane < 4 + nst)
+          bulk_g2s(sb + (lane - 4) * kStepBytesB, B + (long long)(ks + lane - 4) * bstep,
+                   (uint32_t)(gb * 256), &ctl->full[stage]);
+        __syncwarp();
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
-      // every issued copy has landed before the CTA may exit
+      if (!ok) break;
+    }
+    // every issued copy has landed before the CTA may exit
+    if (lane == 0)
       for (int s = 0; s < kStages; ++s)
         if (armed & (1u << s)) {
           const uint64_t deadline = global_timer_ns() + kWaitNs;
           int dummy_abort = 0;
           mbar_wait(&ctl->full[s], (last_par >> s) & 1u, deadline, &dummy_abort);
         }
-    }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc = idesc_i8(kGemmBM, kGemmBN);
+      constexpr uint32_t idesc128 = idesc_i8(kGemmBM, 128), idesc256 = idesc_i8(kGemmBM, 256);
       int stage = 0;
       uint32_t phase = 0;
       int buf = 0;
@@ -525,19 +537,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (long long t = blockIdx.x; t < total_tiles && !ctl->abort; t += gridDim.x) {
         const TileInfo ti = decode_tile(jobs, prefix, num, t);
         const int ksteps = ti.job->ksteps;
+        const uint32_t idesc = ti.job->bn == 256 ? idesc256 : idesc128;
         if (!bounded_wait(&ctl->acc_empty[buf], acc_phase ^ 1u, ctl, cnt)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + (uint32_t)(buf * kGemmBN);
+        const uint32_t d_tmem = tmem + (uint32_t)(buf * kGemmBNMax);
         bool ok = true;
         for (int ks = 0; ks < ksteps; ks += 4) {
           const int nst = min(4, ksteps - ks);
           if (!bounded_wait(&ctl->full[stage], phase, ctl, cnt)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_addr(smem + stage * kStageBytes);
-          const uint32_t sb = sa + 4 * kStepBytes;
+          const uint32_t sb = sa + 4 * kStepBytesA;
           for (int j = 0; j < nst; ++j) {
-            const uint64_t ad = smem_desc_sw32(sa + j * kStepBytes, 256);
-            const uint64_t bd = smem_desc_sw32(sb + j * kStepBytes, 256);
+            const uint64_t ad = smem_desc_sw32(sa + j * kStepBytesA, 256);
+            const uint64_t bd = smem_desc_sw32(sb + j * kStepBytesB, 256);
             mma_i8(d_tmem, ad, bd, idesc, (ks > 0 || j > 0) ? 1u : 0u);
           }
           issued = true;
@@ -576,13 +589,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const int row = ti.tm * kGemmBM + quad * 32 + lane;
       int32_t* C = jb.C + (long long)ti.plane * jb.c_plane;
-      const uint32_t taddr = tmem + (uint32_t)(buf * kGemmBN) + ((uint32_t)(quad * 32) << 16);
+      const uint32_t taddr = tmem + (uint32_t)(buf * kGemmBNMax) + ((uint32_t)(quad * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < kGemmBN / 32; ++c) {
+      for (int c = 0; c < jb.bn / 32; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
         tmem_ld_wait();
-        const int col0 = ti.tn * kGemmBN + c * 32;
+        const int col0 = ti.tn * jb.bn + c * 32;
         if (row < jb.m) {
           int32_t* cp = C + row + (long long)col0 * jb.m;
           const int ncol = min(32, jb.n - col0);
@@ -603,7 +616,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 // ======================================================================= reconstruct kernel

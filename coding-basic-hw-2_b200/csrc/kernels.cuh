@@ -32,9 +32,19 @@ struct GemmJob {
   long long a_plane, b_plane, c_plane;
   int m, n, ksteps, planes;
   int rga, rgb, tm, tn;  // row groups of A / B, tile rows / columns
+  int bn;                // tile width: 256 columns, or 128 for n <= 128
 };
 
-constexpr int kGemmBM = 128, kGemmBN = 128;
+constexpr int kGemmBM = 128, kGemmBNMax = 256;
+
+// Tile shape of one problem: 128 rows x 256 columns (128 when n <= 128); requires m, n set.
+inline void set_gemm_tiling(GemmJob& j) {
+  j.bn = j.n > 128 ? 256 : 128;
+  j.tm = (j.m + kGemmBM - 1) / kGemmBM;
+  j.tn = (j.n + j.bn - 1) / j.bn;
+  j.rga = (j.m + 7) / 8;
+  j.rgb = (j.n + 7) / 8;
+}
 constexpr int kPrepThreads = 256, kReconThreads = 256, kReconPerThread = 4;
 
 // Blocks of one prep descriptor (A: 32 rows per block, B: 8 columns per block).

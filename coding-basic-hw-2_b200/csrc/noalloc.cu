@@ -168,10 +168,7 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
   j.n = q.n;
   j.ksteps = (q.k + 31) / 32;
   j.planes = (emulate && q.k > 0) ? N + 1 : 0;
-  j.rga = (q.m + 7) / 8;
-  j.rgb = (q.n + 7) / 8;
-  j.tm = (q.m + kGemmBM - 1) / kGemmBM;
-  j.tn = (q.n + kGemmBN - 1) / kGemmBN;
+  set_gemm_tiling(j);
   d.job_prefix[0] = 0;
   d.job_prefix[1] = gemm_tiles(j);
   ggemm_recon_desc_t& rc = d.recon;

@@ -97,10 +97,7 @@ extern "C" int ggemm_stage_gemm(const ggemm_gemm_desc_t* descs, int num, void* s
     j.n = d.n;
     j.ksteps = (d.k + 31) / 32;
     j.planes = (d.m > 0 && d.n > 0 && d.k > 0) ? d.planes : 0;
-    j.rga = (d.m + 7) / 8;
-    j.rgb = (d.n + 7) / 8;
-    j.tm = (d.m + kGemmBM - 1) / kGemmBM;
-    j.tn = (d.n + kGemmBN - 1) / kGemmBN;
+    set_gemm_tiling(j);
     if (j.planes > 0) {
       if (!d.A || !d.B || !d.C || ((uintptr_t)d.A & 15) || ((uintptr_t)d.B & 15) ||
           ((uintptr_t)d.C & 3) || (d.a_plane & 15) || (d.b_plane & 15))
