@@ -110,7 +110,7 @@ class GemmDesc(ctypes.Structure):
 
     _fields_ = [("A", c_void_p), ("B", c_void_p), ("C", c_void_p), ("a_plane", c_longlong),
                 ("b_plane", c_longlong), ("c_plane", c_longlong), ("m", c_int), ("n", c_int),
-                ("k", c_int), ("planes", c_int)]
+                ("k", c_int), ("planes", c_int), ("N", c_int), ("layout", c_int)]
 
 
 class ReconDesc(ctypes.Structure):
@@ -119,7 +119,19 @@ class ReconDesc(ctypes.Structure):
     _fields_ = [("m", c_int), ("n", c_int), ("k", c_int), ("N", c_int),
                 ("A", c_void_p), ("lda", c_longlong), ("B", c_void_p), ("ldb", c_longlong),
                 ("C", c_void_p), ("ldc", c_longlong), ("alpha", c_double), ("beta", c_double),
-                ("C32", c_void_p), ("c_plane", c_longlong), ("rs", c_void_p), ("cs", c_void_p)]
+                ("C32", c_void_p), ("c_plane", c_longlong), ("rs", c_void_p), ("cs", c_void_p),
+                ("layout", c_int), ("reserved", c_int)]
+
+
+# Product layouts between the residue GEMM and the reconstruct (ggemm_stages.h).
+PRODUCTS_INT32 = 0
+PRODUCTS_DIGITS = 1
+
+
+def digit_plane_bytes(m, n):
+    """ggemm_digit_plane_bytes: bytes of one digit plane of an m x n problem."""
+    return ((n + 31) // 32 * m * 32 + 255) // 256 * 256
+
 
 
 COUNTER_BYTES = 64

@@ -147,11 +147,10 @@ void print_ws_diag(ggemm_handle_t h, const ggemm_problem_t& p, int N) {
   h->ws_diag_printed = 1;
   std::fprintf(stderr,
                "[ggemm] GGEMM_ERR_WORKSPACE: one problem (m=%d n=%d k=%d, %d moduli) needs "
-               "%zu + %zu residue bytes and %zu int32 products; the handle holds %zu + %zu "
-               "bytes and %zu products (create with larger budgets or min_k <= %d)\n",
+               "%zu + %zu residue bytes and %zu product bytes; the handle holds %zu + %zu "
+               "and %zu bytes (create with larger budgets or min_k <= %d)\n",
                p.m, p.n, p.k, N, img_bytes(p.m, p.k, N), img_bytes(p.n, p.k, N),
-               (size_t)(N + 1) * c_plane_elems(p.m, p.n), h->imgA_cap, h->imgB_cap, h->c32_cap,
-               p.k);
+               4 * product_elems(p.m, p.n, N), h->imgA_cap, h->imgB_cap, 4 * h->c32_cap, p.k);
 }
 
 }  // namespace
@@ -247,7 +246,7 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         const size_t nb = new_b ? img_bytes(p.n, p.k, h->ub_n[ub]) : 0;
         const size_t nwa = new_a ? ws_ints(p.m) : 0;
         const size_t nwb = new_b ? ws_ints(p.n) : 0;
-        const size_t ncc = (size_t)(N + 1) * c_plane_elems(p.m, p.n);
+        const size_t ncc = product_elems(p.m, p.n, N);
         const bool fits = ia + na <= h->imgA_cap && ib + nb <= h->imgB_cap &&
                           wa + nwa <= h->wsA_cap && wb + nwb <= h->wsB_cap &&
                           cc + ncc <= h->c32_cap;
@@ -382,9 +381,13 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       base.A = h->imgA + h->ua_img[ua];
       base.B = h->imgB + h->ub_img[ub];
       base.C = h->c32 + h->c32_off[j];
+      base.Y = reinterpret_cast<uint8_t*>(base.C);
       base.a_plane = (long long)align_up(ggemm_img_plane_bytes(p.m, p.k), kAlign);
       base.b_plane = (long long)align_up(ggemm_img_plane_bytes(p.n, p.k), kAlign);
       base.c_plane = (long long)c_plane_elems(p.m, p.n);
+      base.y_plane = (long long)y8_plane_bytes(p.m, p.n);
+      base.N = N;
+      base.y8 = use_y8(p.m, p.n, N) ? 1 : 0;
       base.m = p.m;
       base.n = p.n;
       base.ksteps = (p.k + 31) / 32;
@@ -394,7 +397,8 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
           GemmJob jb = base;
           jb.A += l * base.a_plane;
           jb.B += l * base.b_plane;
-          jb.C += l * base.c_plane;
+          if (base.y8) jb.plane0 = l;
+          else jb.C += l * base.c_plane;
           jb.planes = 1;
           jobs[jq] = jb;
           jp[2 * jq] = 0;
@@ -417,7 +421,10 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       const int j = ch.first + x;
       const int g = emu[j];
       const ggemm_problem_t& p = probs[g];
+      const bool y8 = use_y8(p.m, p.n, plan[g].num_moduli);
       ggemm_recon_desc_t& d = rd[x];
+      d = ggemm_recon_desc_t{};
+      d.layout = y8 ? GGEMM_PRODUCTS_DIGITS : GGEMM_PRODUCTS_INT32;
       d.m = p.m;
       d.n = p.n;
       d.k = p.k;
@@ -431,11 +438,11 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       d.alpha = p.alpha;
       d.beta = p.beta;
       d.C32 = h->c32 + h->c32_off[j];
-      d.c_plane = (long long)c_plane_elems(p.m, p.n);
+      d.c_plane = y8 ? (long long)y8_plane_bytes(p.m, p.n) : (long long)c_plane_elems(p.m, p.n);
       d.rs = h->wsA + h->ua_ws[h->ua_of[j]];
       d.cs = h->wsB + h->ub_ws[h->ub_of[j]];
       rp[x] = rb;
-      rb += recon_blocks(d);
+      rb += recon_job_blocks(d);
     }
     rp[ch.count] = rb;
     ch.recon_blocks = rb;

@@ -19,6 +19,11 @@ namespace g2 {
 constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline size_t c_plane_elems(int m, int n) { return align_up((size_t)m * (size_t)n, 64); }
+// int32 elements of one problem's products in the layout use_y8 picks (kernels.cuh),
+// 256-byte aligned.
+inline size_t product_elems(int m, int n, int N) {
+  return align_up(use_y8(m, n, N) ? y8_bytes(m, n, N) : c32_bytes(m, n, N), kAlign) / 4;
+}
 inline size_t ws_ints(int rows) { return align_up(4 * (size_t)rows, 64); }
 // Bytes of all planes (N residue planes + abs plane) of one operand image.
 inline size_t img_bytes(int rows, int k, int N) {

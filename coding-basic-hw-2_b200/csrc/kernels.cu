@@ -4,9 +4,9 @@
 //                 (ggemm_stages.h); HBM / integer-ALU bound.
 //   gemm_kernel   persistent tcgen05.mma.kind::i8 GEMM over every (problem, plane, tile):
 //                 bulk copies -> shared-memory ring (mbarriers) -> TMEM int32 accumulators ->
-//                 epilogue warps write int32 products; tensor-core bound.
-//   recon_kernel  CRT reconstruction, unscaling, alpha/beta, componentwise certificate and
-//                 FP64 repair; HBM bound.
+//                 epilogue warps write CRT digit bytes (or int32 products); tensor-core bound.
+//   recon_kernel  CRT reconstruction from digit bytes (or int32 products), unscaling,
+//                 alpha/beta, componentwise certificate and FP64 repair; HBM bound.
 // The numerical definitions (what is computed, bit for bit) are those of the reference
 // src/ozaki2_numerics.cu:8-76 and :112-586; the work decomposition is this library's own.
 #include <cuda_runtime.h>
@@ -444,6 +444,57 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, Gem
   return false;
 }
 
+// CRT digit of an int32 product for one residue plane (the reference computes the same digit
+// inside its reconstruct, src/ozaki2_numerics.cu:509-517).  With u = c + 2^31 (unsigned),
+// magic = floor(2^32 / p) and p odd or 256:
+//   r = u - umulhi(u, magic) p            in [0, 2p), r = c + 2^31 (mod p)
+//   x = r q + corr                        < 2^17, corr = (p - 2^31 mod p) q mod p, x = c q (mod p)
+//   y = x - umulhi(x, magic) p            in [0, 2p), then min(y, y - p) (unsigned) in [0, p)
+// umulhi(u, magic) undershoots floor(u / p) by at most one for every u < 2^32.
+struct DigitCtx {
+  uint32_t p, magic, q, corr;
+  bool digit;  // false: the abs plane (int32 output)
+};
+
+__device__ __forceinline__ DigitCtx digit_ctx(int plane, int N) {
+  DigitCtx dc{1u, 0u, 0u, 0u, plane < N};
+  if (dc.digit) {
+    dc.p = c_tab.p[plane];
+    dc.magic = c_tab.magic[plane];
+    dc.q = c_tab.qinv[N][plane];
+    dc.corr = (dc.p - 0x80000000u % dc.p) % dc.p * dc.q % dc.p;
+  }
+  return dc;
+}
+
+__device__ __forceinline__ uint32_t crt_digit(uint32_t c, const DigitCtx& dc) {
+  const uint32_t u = c ^ 0x80000000u;
+  const uint32_t r = u - __umulhi(u, dc.magic) * dc.p;
+  const uint32_t x = r * dc.q + dc.corr;
+  const uint32_t y = x - __umulhi(x, dc.magic) * dc.p;
+  return min(y, y - dc.p);
+}
+
+// One 32-column record of one row: 32 digit bytes (two 16-byte stores) or 32 int32 (eight).
+__device__ __forceinline__ void emit_record(const uint32_t (&v)[32], const DigitCtx& dc,
+                                            uint8_t* ydst, int32_t* ldst) {
+  if (dc.digit) {
+    uint32_t w[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      w[g] = crt_digit(v[4 * g], dc) | (crt_digit(v[4 * g + 1], dc) << 8) |
+             (crt_digit(v[4 * g + 2], dc) << 16) | (crt_digit(v[4 * g + 3], dc) << 24);
+    uint4* d = reinterpret_cast<uint4*>(ydst);
+    d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  } else {
+    int4* d = reinterpret_cast<int4*>(ldst);
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      d[g] = make_int4((int)v[4 * g], (int)v[4 * g + 1], (int)v[4 * g + 2], (int)v[4 * g + 3]);
+  }
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const GemmJob* __restrict__ jobs, const long long* __restrict__ prefix, int num,
                 long long total_tiles, DevCounters* cnt) {
@@ -588,20 +639,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const int row = ti.tm * kGemmBM + quad * 32 + lane;
-      int32_t* C = jb.C + (long long)ti.plane * jb.c_plane;
       const uint32_t taddr = tmem + (uint32_t)(buf * kGemmBNMax) + ((uint32_t)(quad * 32) << 16);
+      // record columns of this tile that lie inside the problem
+      const int nch = min(jb.bn, jb.n - ti.tn * jb.bn + 31) / 32;
+      if (jb.y8) {
+        const int pl = jb.plane0 + ti.plane;
+        const DigitCtx dc = digit_ctx(pl, jb.N);
+        const long long rec0 = ((long long)ti.tn * (jb.bn / 32) * jb.m + row) * 32;
+        uint8_t* ydst = jb.Y + (long long)pl * jb.y_plane + rec0;
+        int32_t* ldst = reinterpret_cast<int32_t*>(jb.Y + (long long)jb.N * jb.y_plane) + rec0;
+        const long long cstep = (long long)jb.m * 32;  // one record column
+        const bool live = row < jb.m;
+        // two register buffers: the TMEM load of chunk c + 1 overlaps the digits of chunk c
+        uint32_t va[32], vb[32];
+        tmem_ld_32x32b_x32(taddr, va);
+        tmem_ld_wait(va);
 #pragma unroll 1
-      for (int c = 0; c < jb.bn / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
-        tmem_ld_wait();
-        const int col0 = ti.tn * jb.bn + c * 32;
-        if (row < jb.m) {
-          int32_t* cp = C + row + (long long)col0 * jb.m;
-          const int ncol = min(32, jb.n - col0);
+        for (int c = 0; c < nch; c += 2) {
+          if (c + 1 < nch) tmem_ld_32x32b_x32(taddr + (uint32_t)((c + 1) * 32), vb);
+          if (live) emit_record(va, dc, ydst + c * cstep, ldst + c * cstep);
+          if (c + 1 < nch) {
+            tmem_ld_wait(vb);
+            if (c + 2 < nch) tmem_ld_32x32b_x32(taddr + (uint32_t)((c + 2) * 32), va);
+            if (live) emit_record(vb, dc, ydst + (c + 1) * cstep, ldst + (c + 1) * cstep);
+            if (c + 2 < nch) tmem_ld_wait(va);
+          }
+        }
+      } else {
+        int32_t* C = jb.C + (long long)ti.plane * jb.c_plane;
+#pragma unroll 1
+        for (int c = 0; c < nch; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
+          tmem_ld_wait(v);
+          const int col0 = ti.tn * jb.bn + c * 32;
+          if (row < jb.m) {
+            int32_t* cp = C + row + (long long)col0 * jb.m;
+            const int ncol = min(32, jb.n - col0);
 #pragma unroll
-          for (int x = 0; x < 32; ++x)
-            if (x < ncol) cp[(long long)x * jb.m] = (int32_t)v[x];
+            for (int x = 0; x < 32; ++x)
+              if (x < ncol) cp[(long long)x * jb.m] = (int32_t)v[x];
+          }
         }
       }
       tc_fence_before();
@@ -776,7 +854,7 @@ __device__ __forceinline__ void recon_pair(const ggemm_recon_desc_t& d, const Re
   int2 c2[kMaxModuli + 1];
   const int2* __restrict__ src = reinterpret_cast<const int2*>(d.C32 + e0);
   const long long pst = d.c_plane >> 1;
-  const bool need_planes = d.alpha != 0.0;
+  const bool need_planes = d.alpha != 0.0 && d.k > 0;  // k == 0: every entry is special
   if (need_planes) {
 #pragma unroll
     for (int l = 0; l <= kMaxModuli; ++l)
@@ -819,40 +897,10 @@ __device__ __forceinline__ void recon_pair(const ggemm_recon_desc_t& d, const Re
   }
 }
 
-__global__ void __launch_bounds__(kReconThreads, 2) recon_kernel(const ggemm_recon_desc_t* __restrict__ descs,
-                                                              const long long* __restrict__ prefix,
-                                                              int num, int mode,
-                                                              DevCounters* cnt) {
-  const int owner = find_owner(prefix, num, (long long)blockIdx.x);
-  const ggemm_recon_desc_t d = descs[owner];
-  unsigned n_unc = 0, n_rep = 0, n_saf = 0;
-  if (d.N >= 1 && d.N <= kMaxModuli && d.m > 0 && d.n > 0) {
-    const ReconCtx cx = recon_ctx(d);
-    const long long mn = (long long)d.m * d.n;
-    const long long base =
-        ((long long)blockIdx.x - prefix[owner]) * (kReconThreads * kReconPerThread);
-    const bool vec = (d.m & 1) == 0 && (d.c_plane & 1) == 0 &&
-                     ((uintptr_t)d.C32 & 7) == 0 && ((uintptr_t)d.rs & 7) == 0;
-    if (vec) {
-#pragma unroll 1
-      for (int e = 0; e < kReconPerThread / 2; ++e) {
-        const long long e0 = base + 2 * ((long long)e * kReconThreads + threadIdx.x);
-        if (e0 >= mn) break;
-        const int j = (int)(e0 / d.m);
-        recon_pair(d, cx, mode, e0, (int)(e0 - (long long)j * d.m), j, n_unc, n_rep, n_saf);
-      }
-    } else {
-#pragma unroll 1
-      for (int e = 0; e < kReconPerThread; ++e) {
-        const long long idx = base + e * kReconThreads + threadIdx.x;
-        if (idx >= mn) break;
-        const int j = (int)(idx / d.m);
-        const int i = (int)(idx - (long long)j * d.m);
-        recon_entry(d, cx, mode, idx, i, j, n_unc, n_rep, n_saf);
-      }
-    }
-  }
-  // counters: warp reduce, block reduce, at most one atomic per counter per block
+// Block-level reduction of the three counters: at most one atomic per counter per block.
+// Every thread of the block calls it.
+__device__ __forceinline__ void flush_counters(unsigned n_unc, unsigned n_rep, unsigned n_saf,
+                                               DevCounters* cnt) {
   unsigned long long cu = n_unc, cr = n_rep, cf = n_saf;
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
@@ -878,6 +926,139 @@ __global__ void __launch_bounds__(kReconThreads, 2) recon_kernel(const ggemm_rec
       atomicAdd(dst, t);
     }
   }
+}
+
+// Reconstruct from int32 products: block `local` of the problem takes 1024 consecutive
+// column-major entries, 4 per thread (two pairs when m is even).
+__device__ __forceinline__ void recon_c32_block(const ggemm_recon_desc_t& d, long long local,
+                                                int mode, unsigned& n_unc, unsigned& n_rep,
+                                                unsigned& n_saf) {
+  if (d.N >= 1 && d.N <= kMaxModuli && d.m > 0 && d.n > 0) {
+    const ReconCtx cx = recon_ctx(d);
+    const long long mn = (long long)d.m * d.n;
+    const long long base = local * (kReconThreads * kReconPerThread);
+    const bool vec = (d.m & 1) == 0 && (d.c_plane & 1) == 0 &&
+                     ((uintptr_t)d.C32 & 7) == 0 && ((uintptr_t)d.rs & 7) == 0;
+    if (vec) {
+#pragma unroll 1
+      for (int e = 0; e < kReconPerThread / 2; ++e) {
+        const long long e0 = base + 2 * ((long long)e * kReconThreads + threadIdx.x);
+        if (e0 >= mn) break;
+        const int j = (int)(e0 / d.m);
+        recon_pair(d, cx, mode, e0, (int)(e0 - (long long)j * d.m), j, n_unc, n_rep, n_saf);
+      }
+    } else {
+#pragma unroll 1
+      for (int e = 0; e < kReconPerThread; ++e) {
+        const long long idx = base + e * kReconThreads + threadIdx.x;
+        if (idx >= mn) break;
+        const int j = (int)(idx / d.m);
+        const int i = (int)(idx - (long long)j * d.m);
+        recon_entry(d, cx, mode, idx, i, j, n_unc, n_rep, n_saf);
+      }
+    }
+  }
+}
+
+// Reconstruct from the digit layout.  Block: 64 rows x one 32-column record column; thread t
+// takes row 64 b + t / 4 and the 8 columns 8 (t % 4) .. 8 (t % 4) + 7 of the record, so that a
+// warp reads 256 contiguous bytes of each digit plane per load.  The digit and abs-plane loads
+// of a thread (8 bytes per digit plane, 32 bytes of the abs plane) are all issued before its
+// first entry is reconstructed.  Column statistics are staged in shared memory.
+// Every thread of the block calls it.
+__device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long long local,
+                                               int mode, unsigned& n_unc, unsigned& n_rep,
+                                               unsigned& n_saf) {
+  __shared__ int s_col[4][32];  // csh, tau, ||dB|| bits, ||B'|| bits of the 32 columns
+  const bool ok_desc = d.N >= 1 && d.N <= kMaxModuli && d.m > 0 && d.n > 0;
+  const long long rblocks = ok_desc ? (d.m + kY8Rows - 1) / kY8Rows : 1;
+  const int ch = ok_desc ? (int)(local / rblocks) : 0;
+  const int i = (int)(local - ch * rblocks) * kY8Rows + (threadIdx.x >> 2);
+  const int cg = threadIdx.x & 3;
+  const bool planes = ok_desc && d.alpha != 0.0 && d.k > 0;
+  if (threadIdx.x < 128) {
+    const int st = threadIdx.x >> 5, j = ch * 32 + (threadIdx.x & 31);
+    s_col[st][threadIdx.x & 31] = (ok_desc && d.alpha != 0.0 && j < d.n) ? d.cs[st * d.n + j] : 0;
+  }
+  __syncthreads();
+  if (ok_desc && i < d.m) {
+    const ReconCtx cx = recon_ctx(d);
+    const int N = cx.N;
+    const int j0 = ch * 32 + cg * 8;
+    const int ncol = min(8, d.n - j0);
+    const long long rec = ((long long)ch * d.m + i) * 32 + cg * 8;
+    const uint8_t* Y = reinterpret_cast<const uint8_t*>(d.C32);
+    uint2 yv[kMaxModuli];
+    int4 l0 = make_int4(0, 0, 0, 0), l1 = l0;
+    int rsh = 0, sig = 0;
+    float fda = 0.f, fna = 0.f;
+    if (planes) {
+#pragma unroll
+      for (int l = 0; l < kMaxModuli; ++l)
+        if (l < N) yv[l] = __ldg(reinterpret_cast<const uint2*>(Y + l * d.c_plane + rec));
+      const int4* lp = reinterpret_cast<const int4*>(
+          reinterpret_cast<const int32_t*>(Y + (long long)N * d.c_plane) + rec);
+      l0 = __ldg(lp);
+      l1 = __ldg(lp + 1);
+    }
+    if (d.alpha != 0.0) {
+      rsh = __ldg(d.rs + i);
+      sig = __ldg(d.rs + d.m + i);
+      fda = __int_as_float(__ldg(d.rs + 2 * d.m + i));
+      fna = __int_as_float(__ldg(d.rs + 3 * d.m + i));
+    }
+    double* crow = d.C + i + (long long)j0 * d.ldc;
+    if (d.beta != 0.0)  // the second half's entries of C, fetched while the first is computed
+      for (int x = 4; x < ncol; ++x) prefetch_l2(crow + x * d.ldc);
+    // two halves of 4 entries: the digits of a half are bytes of one 32-bit word per plane
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      const int xb = 4 * h;
+      if (xb >= ncol) break;
+      double c0[4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+        c0[x] = (d.beta != 0.0 && xb + x < ncol) ? crow[(xb + x) * d.ldc] : 0.0;
+      uint32_t yw[kMaxModuli];
+#pragma unroll
+      for (int l = 0; l < kMaxModuli; ++l) yw[l] = h ? yv[l].y : yv[l].x;
+      const int4 lq = h ? l1 : l0;
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        if (xb + x >= ncol) break;
+        double* cp = crow + (xb + x) * d.ldc;
+        const int cx8 = cg * 8 + xb + x;
+        const int csh = s_col[0][cx8], tau = s_col[1][cx8];
+        if (recon_special(d, i, j0 + xb + x, cp, c0[x], rsh, csh, sig, tau, n_saf)) continue;
+        uint64_t S1 = 0;
+        uint32_t S2 = 0;
+#pragma unroll
+        for (int l = 0; l < kMaxModuli; ++l) {
+          if (l >= N) break;
+          const uint32_t y = (yw[l] >> (8 * x)) & 255u;
+          S1 += c_tab.s1[N][l] * (uint64_t)y;
+          S2 += c_tab.s2[N][l] * y;
+        }
+        const int32_t L = x == 0 ? lq.x : x == 1 ? lq.y : x == 2 ? lq.z : lq.w;
+        recon_finish(d, cx, mode, i, j0 + xb + x, cp, c0[x], S1, S2, L, rsh, csh, sig, tau, fda,
+                     fna, __int_as_float(s_col[2][cx8]), __int_as_float(s_col[3][cx8]), n_unc,
+                     n_rep);
+      }
+    }
+  }
+}
+
+// One launch over every problem of a call; the layout is chosen per problem (block-uniform).
+__global__ void __launch_bounds__(kReconThreads, 2)
+    recon_kernel(const ggemm_recon_desc_t* __restrict__ descs,
+                 const long long* __restrict__ prefix, int num, int mode, DevCounters* cnt) {
+  const int owner = find_owner(prefix, num, (long long)blockIdx.x);
+  const ggemm_recon_desc_t d = descs[owner];
+  const long long local = (long long)blockIdx.x - prefix[owner];
+  unsigned n_unc = 0, n_rep = 0, n_saf = 0;
+  if (d.layout == GGEMM_PRODUCTS_DIGITS) recon_y8_block(d, local, mode, n_unc, n_rep, n_saf);
+  else recon_c32_block(d, local, mode, n_unc, n_rep, n_saf);
+  flush_counters(n_unc, n_rep, n_saf, cnt);
 }
 
 // ===================================================================================== host
@@ -939,7 +1120,8 @@ int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix, i
                  long long total_blocks, int mode, DevCounters* cnt, cudaStream_t s) {
   if (num <= 0 || total_blocks <= 0) return 0;
   if (total_blocks > 0x7FFFFFFFLL) return (int)cudaErrorInvalidConfiguration;
-  recon_kernel<<<(unsigned)total_blocks, kReconThreads, 0, s>>>(d_descs, d_prefix, num, mode, cnt);
+  recon_kernel<<<(unsigned)total_blocks, kReconThreads, 0, s>>>(d_descs, d_prefix, num, mode,
+                                                                cnt);
   return (int)cudaGetLastError();
 }
 

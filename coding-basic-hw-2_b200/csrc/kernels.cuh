@@ -24,15 +24,32 @@ enum : unsigned int {
   kStatusGemmTimeout = 1,  // a residue-GEMM pipeline wait ran past its deadline
 };
 
+// Digit layout ("Y8", GGEMM_PRODUCTS_DIGITS in ggemm_stages.h) of the products handed from the
+// GEMM to the reconstruct: an epilogue lane (one row) writes 32 contiguous bytes per digit
+// plane, and a reconstruct thread reads 8 columns of one plane with one 8-byte load.
+inline size_t y8_plane_bytes(int m, int n) { return ggemm_digit_plane_bytes(m, n); }
+inline size_t y8_bytes(int m, int n, int N) {
+  return (size_t)N * y8_plane_bytes(m, n) + 4 * y8_plane_bytes(m, n);
+}
+// int32 layout: N + 1 planes of m * n products (column-major), each padded to 64 elements.
+inline size_t c32_bytes(int m, int n, int N) {
+  return 4 * (size_t)(N + 1) * (((size_t)m * (size_t)n + 63) / 64 * 64);
+}
+// The digit layout is used whenever it is no larger than the int32 layout (it is larger only
+// for n below about 10, where the 32-column records are mostly padding).
+inline bool use_y8(int m, int n, int N) { return y8_bytes(m, n, N) <= c32_bytes(m, n, N); }
+
 // One problem of the residue GEMM as the kernel sees it (built on the host).
 struct GemmJob {
   const int8_t* A;
   const int8_t* B;
-  int32_t* C;
-  long long a_plane, b_plane, c_plane;
+  int32_t* C;            // int32 products (y8 == 0)
+  uint8_t* Y;            // digit layout (y8 == 1)
+  long long a_plane, b_plane, c_plane, y_plane;
   int m, n, ksteps, planes;
   int rga, rgb, tm, tn;  // row groups of A / B, tile rows / columns
   int bn;                // tile width: 256 columns, or 128 for n <= 128
+  int N, plane0, y8;     // moduli, index of the job's first plane, output layout
 };
 
 constexpr int kGemmBM = 128, kGemmBNMax = 256;
@@ -57,6 +74,16 @@ inline long long recon_blocks(const ggemm_recon_desc_t& d) {
   const long long per = (long long)kReconThreads * kReconPerThread;
   return (mn + per - 1) / per;
 }
+// Digit-layout reconstruct: one block per 64 rows x 32 columns (one record column).
+constexpr int kY8Rows = 64;
+inline long long recon_blocks_y8(const ggemm_recon_desc_t& d) {
+  if (d.m <= 0 || d.n <= 0) return 0;
+  return (long long)((d.n + 31) / 32) * ((d.m + kY8Rows - 1) / kY8Rows);
+}
+// Blocks of one reconstruct descriptor in its layout.
+inline long long recon_job_blocks(const ggemm_recon_desc_t& d) {
+  return d.layout == GGEMM_PRODUCTS_DIGITS ? recon_blocks_y8(d) : recon_blocks(d);
+}
 inline long long gemm_tiles(const GemmJob& j) { return (long long)j.tm * j.tn * j.planes; }
 
 // Uploads the CRT constants to the current device (once per device; thread-safe).
@@ -70,6 +97,7 @@ int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, int num, 
                 DevCounters* cnt, cudaStream_t s);
 int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long long total_tiles,
                 DevCounters* cnt, cudaStream_t s);
+// Blocks per job: recon_job_blocks.
 int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix, int num,
                  long long total_blocks, int mode, DevCounters* cnt, cudaStream_t s);
 

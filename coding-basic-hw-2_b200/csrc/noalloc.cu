@@ -108,16 +108,18 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
                                                        : GGEMM_STAGE_REPAIR_ON;
   const bool emulate = q.alpha != 0.0;  // alpha == 0: C = beta C without reading A or B
 
-  // scratch layout: counters | descriptors | ws A | ws B | image A | image B | C32
+  // scratch layout: counters | descriptors | ws A | ws B | image A | image B | products
   const size_t pa = up256(ggemm_img_plane_bytes(q.m, q.k));
   const size_t pb = up256(ggemm_img_plane_bytes(q.n, q.k));
   const size_t cp = ((size_t)q.m * q.n + 63) / 64 * 64;
+  const bool digits = use_y8(q.m, q.n, N);
+  const size_t prod = digits ? y8_bytes(q.m, q.n, N) : c32_bytes(q.m, q.n, N);
   const size_t off_wa = kOffData;
   const size_t off_wb = off_wa + up256(16 * (size_t)q.m);
   const size_t off_ia = off_wb + up256(16 * (size_t)q.n);
   const size_t off_ib = off_ia + (emulate ? (size_t)(N + 1) * pa : 0);
   const size_t off_c = off_ib + (emulate ? (size_t)(N + 1) * pb : 0);
-  const size_t need = off_c + (emulate && q.k > 0 ? (size_t)(N + 1) * cp * 4 : 0);
+  const size_t need = off_c + (emulate && q.k > 0 ? prod : 0);
   if (need > kNoAllocBytes) {
     std::fprintf(stderr,
                  "[ggemm] ggemm_dgemm_noalloc: m=%d n=%d k=%d with %d moduli needs %zu bytes of "
@@ -161,9 +163,13 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
   j.A = reinterpret_cast<const int8_t*>(base + off_ia);
   j.B = reinterpret_cast<const int8_t*>(base + off_ib);
   j.C = reinterpret_cast<int32_t*>(base + off_c);
+  j.Y = base + off_c;
   j.a_plane = (long long)pa;
   j.b_plane = (long long)pb;
   j.c_plane = (long long)cp;
+  j.y_plane = (long long)y8_plane_bytes(q.m, q.n);
+  j.N = N;
+  j.y8 = digits ? 1 : 0;
   j.m = q.m;
   j.n = q.n;
   j.ksteps = (q.k + 31) / 32;
@@ -185,11 +191,12 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
   rc.alpha = q.alpha;
   rc.beta = q.beta;
   rc.C32 = reinterpret_cast<const int32_t*>(base + off_c);
-  rc.c_plane = (long long)cp;
+  rc.c_plane = digits ? (long long)y8_plane_bytes(q.m, q.n) : (long long)cp;
+  rc.layout = digits ? GGEMM_PRODUCTS_DIGITS : GGEMM_PRODUCTS_INT32;
   rc.rs = reinterpret_cast<const int32_t*>(base + off_wa);
   rc.cs = reinterpret_cast<const int32_t*>(base + off_wb);
   d.recon_prefix[0] = 0;
-  d.recon_prefix[1] = recon_blocks(rc);
+  d.recon_prefix[1] = recon_job_blocks(rc);
 
   const unsigned char* db = base + kOffDescs;
   DevCounters* cnt = reinterpret_cast<DevCounters*>(base + kOffCounters);

@@ -86,25 +86,34 @@ extern "C" int ggemm_stage_gemm(const ggemm_gemm_desc_t* descs, int num, void* s
     const ggemm_gemm_desc_t& d = descs[i];
     if (d.m < 0 || d.n < 0 || d.k < 0 || d.planes < 0 || d.k > kMaxKExact)
       return GGEMM_ERR_INVALID;
+    const bool digits = d.layout == GGEMM_PRODUCTS_DIGITS;
+    if (!digits && d.layout != GGEMM_PRODUCTS_INT32) return GGEMM_ERR_INVALID;
     GemmJob j{};
     j.A = d.A;
     j.B = d.B;
     j.C = d.C;
+    j.Y = reinterpret_cast<uint8_t*>(d.C);
     j.a_plane = d.a_plane;
     j.b_plane = d.b_plane;
     j.c_plane = d.c_plane;
+    j.y_plane = d.c_plane;
     j.m = d.m;
     j.n = d.n;
     j.ksteps = (d.k + 31) / 32;
     j.planes = (d.m > 0 && d.n > 0 && d.k > 0) ? d.planes : 0;
+    j.N = d.N;
+    j.y8 = digits ? 1 : 0;
     set_gemm_tiling(j);
     if (j.planes > 0) {
       if (!d.A || !d.B || !d.C || ((uintptr_t)d.A & 15) || ((uintptr_t)d.B & 15) ||
-          ((uintptr_t)d.C & 3) || (d.a_plane & 15) || (d.b_plane & 15))
+          ((uintptr_t)d.C & (digits ? 15 : 3)) || (d.a_plane & 15) || (d.b_plane & 15))
         return GGEMM_ERR_INVALID;
       if ((size_t)d.a_plane < ggemm_img_plane_bytes(d.m, d.k) ||
-          (size_t)d.b_plane < ggemm_img_plane_bytes(d.n, d.k) ||
-          d.c_plane < (long long)d.m * d.n)
+          (size_t)d.b_plane < ggemm_img_plane_bytes(d.n, d.k))
+        return GGEMM_ERR_INVALID;
+      if (digits ? (d.N < 1 || d.N > kMaxModuli || d.planes > d.N + 1 || (d.c_plane & 15) ||
+                    (size_t)d.c_plane < ggemm_digit_plane_bytes(d.m, d.n))
+                 : d.c_plane < (long long)d.m * d.n)
         return GGEMM_ERR_INVALID;
     }
     jobs[i] = j;
@@ -139,8 +148,15 @@ extern "C" int ggemm_stage_recon(const ggemm_recon_desc_t* descs, int num, int r
   for (int i = 0; i < num; ++i) {
     const ggemm_recon_desc_t& d = descs[i];
     if (d.m < 0 || d.n < 0 || d.k < 0 || d.N < 1 || d.N > kMaxModuli) return GGEMM_ERR_INVALID;
+    if (d.layout == GGEMM_PRODUCTS_DIGITS) {
+      if (((uintptr_t)d.C32 & 15) || (d.c_plane & 15) ||
+          (size_t)d.c_plane < ggemm_digit_plane_bytes(d.m, d.n))
+        return GGEMM_ERR_INVALID;
+    } else if (d.layout != GGEMM_PRODUCTS_INT32) {
+      return GGEMM_ERR_INVALID;
+    }
     pre[i] = blocks;
-    blocks += recon_blocks(d);
+    blocks += recon_job_blocks(d);
   }
   pre[num] = blocks;
   int r = copy_blob(scratch, scratch_bytes, bytes, s);

@@ -45,13 +45,13 @@ int ggemm_shard_group(const ggemm_problem_t* problems, int num, int num_shards,
  * device), for callers that cannot allocate device memory: code that owns no CUDA allocator,
  * runs inside another runtime's memory pool, or must not call cudaMalloc / cudaFree.  It has
  * no counterpart in the reference.  The caller passes inputs and outputs; all scratch (residue
- * images, int32 products, workspace, descriptors, counters) lives in one fixed 64 MiB device
+ * images, products, workspace, descriptors, counters) lives in one fixed 64 MiB device
  * array compiled into this library, which every GPU that loads the library holds until exit.
  * Nothing is allocated: no cudaMalloc / cudaFree, no allocating library routine.
  *   num_moduli: 0 = adaptive (target 1e-15) or a fixed N in [2, 20];
  *   repair_mode: GGEMM_REPAIR_* (default = COUNT, as GGEMM_PATH_EMU_GROUPED).
  * Results equal ggemm_grouped_dgemm(GGEMM_PATH_EMU_GROUPED) of the same problem, bit for bit.
- * A problem whose scratch exceeds 64 MiB (about 830^3 at N = 15) returns GGEMM_ERR_WORKSPACE
+ * A problem whose scratch exceeds 64 MiB (about 1130^3 at N = 15) returns GGEMM_ERR_WORKSPACE
  * with a one-line message on stderr, before anything is enqueued; k > 131040 returns
  * GGEMM_ERR_UNSAFE.
  * The first call on a device does a one-time set-up with that device current (uploads the CRT

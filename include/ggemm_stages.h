@@ -61,19 +61,41 @@ typedef struct {
   int32_t* ws;
 } ggemm_prep_desc_t;
 
-/* One problem of the residue GEMM: for every plane l < planes,
- * C[l*c_plane + i + j*m] = sum_q A_l(i, q) * B_l(j, q) (exact int32), A/B in the image
- * layout above (A: m rows, B: n rows, depth k). */
+/* Products handed from the residue GEMM to the reconstruct (`layout` below).
+ * GGEMM_PRODUCTS_INT32: N+1 planes of m*n int32 products C_l = A_l B_l^T, column-major
+ *   (ld = m), at stride c_plane int32 elements.
+ * GGEMM_PRODUCTS_DIGITS: for residue plane l < N the CRT digit y_l = (C_l mod p_l) q_l mod p_l
+ *   (the value the reconstruct derives from C_l first) as one byte; for the abs plane l = N
+ *   the int32 product.  Both in records of 32 consecutive columns of one row, c_plane in bytes:
+ *     digit y_l(i, j):   byte  at base + l*c_plane + ((j/32)*m + i)*32 + j%32
+ *     abs product (i, j): int32 at ((int32_t*)(base + N*c_plane))[((j/32)*m + i)*32 + j%32]
+ *   c_plane >= ggemm_digit_plane_bytes(m, n) and a multiple of 16; the abs plane takes
+ *   4 * ggemm_digit_plane_bytes(m, n) bytes.  Columns j >= n of the last record are padding.
+ *   N + 4 bytes per entry instead of 4 (N + 1). */
+#define GGEMM_PRODUCTS_INT32 0
+#define GGEMM_PRODUCTS_DIGITS 1
+
+/* Bytes of one digit plane of an m x n problem (256-byte multiple). */
+static inline size_t ggemm_digit_plane_bytes(int m, int n) {
+  const size_t b = (((size_t)n + 31) / 32) * (size_t)m * 32;
+  return (b + 255) / 256 * 256;
+}
+
+/* One problem of the residue GEMM: for every plane l < planes the exact int32 product
+ * C_l(i, j) = sum_q A_l(i, q) * B_l(j, q), A/B in the image layout above (A: m rows, B: n
+ * rows, depth k), stored in `layout` at C (int32 layout: C[l*c_plane + i + j*m]).
+ * N is the number of moduli (digit layout only; planes <= N + 1 there). */
 typedef struct {
   const int8_t* A;
   const int8_t* B;
   int32_t* C;
-  long long a_plane, b_plane, c_plane; /* bytes, bytes, int32 elements */
+  long long a_plane, b_plane, c_plane; /* bytes, bytes, int32 elements (digit layout: bytes) */
   int m, n, k, planes;
+  int N, layout;
 } ggemm_gemm_desc_t;
 
-/* One problem of the reconstruct.  C32: N+1 planes of m*n int32 (column-major, ld = m) at
- * stride c_plane elements; rs / cs: prep workspaces of A (4m) and B (4n). */
+/* One problem of the reconstruct.  C32: the N+1 products in `layout`, c_plane as above;
+ * rs / cs: prep workspaces of A (4m) and B (4n). */
 typedef struct {
   int m, n, k, N;
   const double* A; long long lda;
@@ -83,6 +105,7 @@ typedef struct {
   const int32_t* C32; long long c_plane;
   const int32_t* rs;
   const int32_t* cs;
+  int layout, reserved;
 } ggemm_recon_desc_t;
 
 #define GGEMM_STAGE_REPAIR_OFF 0

@@ -191,3 +191,31 @@ class Reference:
 
 def problem_dict(m, n, k, A, lda, B, ldb, C, ldc, alpha, beta):
     return dict(m=m, n=n, k=k, A=A, lda=lda, B=B, ldb=ldb, C=C, ldc=ldc, alpha=alpha, beta=beta)
+
+
+def decode_tables(buf: bytes):
+    """Decodes the oz2_crt_tables layout."""
+    off = 0
+
+    def take(dtype, count):
+        nonlocal off
+        a = np.frombuffer(buf, dtype=dtype, count=count, offset=off)
+        off += a.nbytes
+        return a
+
+    t = {}
+    t["p"] = take(np.int32, 20)
+    t["magic"] = take(np.uint32, 20)
+    t["pow2"] = take(np.uint8, 20 * 128).reshape(20, 128)
+    t["s1"] = take(np.uint64, 21 * 20).reshape(21, 20)
+    t["s2"] = take(np.uint32, 21 * 20).reshape(21, 20)
+    t["qinv"] = take(np.int32, 21 * 20).reshape(21, 20)
+    off = (off + 7) // 8 * 8
+    t["P1"] = take(np.int64, 21)
+    t["P2"] = take(np.float64, 21)
+    t["inv_Pu"] = take(np.float64, 21)
+    t["log2_u1"] = take(np.int32, 21)
+    off = (off + 7) // 8 * 8
+    t["T"] = take(np.float64, 21)
+    t["log2P"] = take(np.float64, 21)
+    return t

@@ -39,8 +39,8 @@ def test_struct_layouts(g2):
     assert ctypes.sizeof(g2.Config) == 24
     assert ctypes.sizeof(g2.Stats) == 64
     assert ctypes.sizeof(g2.PrepDesc) == 56
-    assert ctypes.sizeof(g2.GemmDesc) == 64
-    assert ctypes.sizeof(g2.ReconDesc) == 112
+    assert ctypes.sizeof(g2.GemmDesc) == 72
+    assert ctypes.sizeof(g2.ReconDesc) == 120
 
 
 def test_struct_sizes_match_reference(g2, ref):

@@ -15,38 +15,13 @@ from fractions import Fraction
 import numpy as np
 import pytest
 
-from g2util import col_major, gen
+from g2util import col_major, decode_tables, gen
 
 MODULI = [256, 255, 253, 251, 247, 239, 233, 229, 227, 223, 217, 211, 199, 197, 193, 191, 181,
           179, 173, 167]
 
 
-def _tables(buf: bytes):
-    """Decodes the oz2_crt_tables layout."""
-    off = 0
-
-    def take(dtype, count):
-        nonlocal off
-        a = np.frombuffer(buf, dtype=dtype, count=count, offset=off)
-        off += a.nbytes
-        return a
-
-    t = {}
-    t["p"] = take(np.int32, 20)
-    t["magic"] = take(np.uint32, 20)
-    t["pow2"] = take(np.uint8, 20 * 128).reshape(20, 128)
-    t["s1"] = take(np.uint64, 21 * 20).reshape(21, 20)
-    t["s2"] = take(np.uint32, 21 * 20).reshape(21, 20)
-    t["qinv"] = take(np.int32, 21 * 20).reshape(21, 20)
-    off = (off + 7) // 8 * 8
-    t["P1"] = take(np.int64, 21)
-    t["P2"] = take(np.float64, 21)
-    t["inv_Pu"] = take(np.float64, 21)
-    t["log2_u1"] = take(np.int32, 21)
-    off = (off + 7) // 8 * 8
-    t["T"] = take(np.float64, 21)
-    t["log2P"] = take(np.float64, 21)
-    return t
+_tables = decode_tables
 
 
 def test_tables_identical_to_reference(oracle, ref):
