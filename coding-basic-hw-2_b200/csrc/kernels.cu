@@ -114,13 +114,17 @@ __device__ __forceinline__ void split_digits(double xt, ElemDigits& e) {
   e.low = neg ? ((0u - lb) & 255u) : lb;
 }
 
-// Symmetric residue of x mod p_l (odd p) as the low byte of a 32-bit word.
+// Symmetric residue of x mod p_l (odd p) as the low byte of a 32-bit word.  The quotient is
+// rounded by adding 1.5 * 2^23 in the same FMA that forms t * fl(1/p): the sum lies in
+// [2^23, 2^24), where the float spacing is 1, so the FMA rounds the exact product to the nearest
+// integer.  That integer is round(t / p) by the bound above (the exact product is even closer to
+// t / p than the rounded one), so all four steps run on the FMA pipe and none is a conversion.
 template <int D>
 __device__ __forceinline__ uint32_t odd_residue_byte(const ElemDigits& e, int l) {
   float t = e.f[0];
 #pragma unroll
   for (int i = 1; i < D; ++i) t = fmaf(e.f[i], c_tab.w[l][i], t);
-  const float q = rintf(t * c_tab.invpf[l]);
+  const float q = fmaf(t, c_tab.invpf[l], 12582912.0f) - 12582912.0f;
   const float s = fmaf(-q, c_tab.pf[l], t);
   return __float_as_uint(s + 12582912.0f);  // low byte = s mod 256 (|s| <= 127)
 }
@@ -752,13 +756,21 @@ __device__ __forceinline__ void crt_sums(const int32_t (&v)[kMaxModuli + 1], int
   }
 }
 
-// Everything after the CRT sums for one entry (src/ozaki2_numerics.cu:519-563).
-__device__ __forceinline__ void recon_finish(const ggemm_recon_desc_t& d, const ReconCtx& cx,
-                                             int mode, int i, int j, double* cp, double c0,
-                                             uint64_t S1, uint32_t S2, int32_t L32, int rsh,
-                                             int csh, int sig, int tau, float fda, float fna,
-                                             float fdb, float fnb, unsigned& n_unc,
-                                             unsigned& n_rep) {
+// Replaces *cp by alpha * r + beta * c0, r the sequential FP64 dot of row i and column j.
+__device__ __forceinline__ void dot_entry(const ggemm_recon_desc_t& d, int i, int j, double* cp,
+                                          double c0) {
+  const double r = fp64_dot(d, i, j);
+  *cp = (d.beta == 0.0) ? d.alpha * r : fma(d.alpha, r, d.beta * c0);
+}
+
+// Everything after the CRT sums for one entry (src/ozaki2_numerics.cu:519-563).  Returns true
+// for an uncertified entry in REPAIR_ON mode, which is left unwritten: the caller repairs it
+// with dot_entry (kept out of this function so that its loop is not inlined per entry).
+__device__ __forceinline__ bool recon_finish(const ggemm_recon_desc_t& d, const ReconCtx& cx,
+                                             int mode, double* cp, double c0, uint64_t S1,
+                                             uint32_t S2, int32_t L32, int rsh, int csh, int sig,
+                                             int tau, double da, double na, double db, double nb,
+                                             unsigned& n_unc) {
   const double alpha = d.alpha, beta = d.beta;
   const int N = cx.N;
   const double s2d = (double)S2 * 0x1p-18;
@@ -770,10 +782,9 @@ __device__ __forceinline__ void recon_finish(const ggemm_recon_desc_t& d, const 
   const double emu = (beta == 0.0) ? alpha * v : fma(alpha, v, beta * c0);
   if (mode == GGEMM_STAGE_REPAIR_OFF || (beta != 0.0 && !isfinite(c0))) {
     *cp = emu;
-    return;
+    return false;
   }
   const double u = 0x1p-53;
-  const double da = fda, na = fna, db = fdb, nb = fnb;
   const double et = fma(da, nb, fma(na, db, da * db)) * (1.0 + 0x1p-40);
   const double Eu = fma(4.0 * u, fabs(xr), fma(et, cx.inv_u1, cx.crt_u)) * (1.0 + 0x1p-40);
   const double E = mul_pow2(Eu, esc);
@@ -784,39 +795,30 @@ __device__ __forceinline__ void recon_finish(const ggemm_recon_desc_t& d, const 
   const double lhs = aalpha * E * (1.0 + 0x1p-40);
   const double rhs = cx.gam * fma(aalpha, lab, fabs(beta * c0)) * (1.0 - 0x1p-40);
   const bool cert = cx.gam > 0.0 && E >= 0x1p-1000 && isfinite(lhs) && isfinite(v) && lhs <= rhs;
-  if (cert) {
+  if (cert || mode == GGEMM_STAGE_REPAIR_COUNT) {
     *cp = emu;
-  } else if (mode == GGEMM_STAGE_REPAIR_COUNT) {
-    *cp = emu;
-    ++n_unc;
-  } else {
-    const double r = fp64_dot(d, i, j);
-    *cp = (beta == 0.0) ? alpha * r : fma(alpha, r, beta * c0);
-    ++n_rep;
+    n_unc += cert ? 0u : 1u;
+    return false;
   }
+  return true;
 }
 
-// The cases that never read the int32 products (src/ozaki2_numerics.cu:492-504).  Returns true
-// when the entry is done.
-__device__ __forceinline__ bool recon_special(const ggemm_recon_desc_t& d, int i, int j,
-                                              double* cp, double c0, int rsh, int csh, int sig,
-                                              int tau, unsigned& n_saf) {
+// The cases that never read the products (src/ozaki2_numerics.cu:492-504).  Returns 0 for an
+// ordinary entry, 1 when the entry is done, 2 for a row or column containing NaN or Inf: the
+// entry is left unwritten and the caller computes it with dot_entry (the safety fallback).
+__device__ __forceinline__ int recon_special(const ggemm_recon_desc_t& d, double* cp, double c0,
+                                             int rsh, int csh, int sig, int tau) {
   const double alpha = d.alpha, beta = d.beta;
   if (alpha == 0.0) {
     *cp = (beta == 0.0) ? 0.0 : beta * c0;
-    return true;
+    return 1;
   }
-  if (rsh == kShiftNonfinite || csh == kShiftNonfinite) {
-    const double v = fp64_dot(d, i, j);
-    *cp = (beta == 0.0) ? alpha * v : fma(alpha, v, beta * c0);
-    ++n_saf;
-    return true;
-  }
+  if (rsh == kShiftNonfinite || csh == kShiftNonfinite) return 2;
   if (sig == kShiftZero || tau == kShiftZero) {
     *cp = (beta == 0.0) ? alpha * 0.0 : fma(alpha, 0.0, beta * c0);
-    return true;
+    return 1;
   }
-  return false;
+  return 0;
 }
 
 // One entry, scalar loads (any m).
@@ -827,7 +829,13 @@ __device__ __forceinline__ void recon_entry(const ggemm_recon_desc_t& d, const R
   const double c0 = (d.beta == 0.0) ? 0.0 : *cp;
   const int rsh = d.alpha == 0.0 ? 0 : d.rs[i], csh = d.alpha == 0.0 ? 0 : d.cs[j];
   const int sig = d.alpha == 0.0 ? 0 : d.rs[d.m + i], tau = d.alpha == 0.0 ? 0 : d.cs[d.n + j];
-  if (recon_special(d, i, j, cp, c0, rsh, csh, sig, tau, n_saf)) return;
+  if (const int sp = recon_special(d, cp, c0, rsh, csh, sig, tau)) {
+    if (sp == 2) {
+      dot_entry(d, i, j, cp, c0);
+      ++n_saf;
+    }
+    return;
+  }
   int32_t v[kMaxModuli + 1];
   const int32_t* __restrict__ C32 = d.C32 + idx;
 #pragma unroll
@@ -840,9 +848,12 @@ __device__ __forceinline__ void recon_entry(const ggemm_recon_desc_t& d, const R
 #pragma unroll
   for (int l = 0; l <= kMaxModuli; ++l)
     if (l == cx.N) L = v[l];
-  recon_finish(d, cx, mode, i, j, cp, c0, S1, S2, L, rsh, csh, sig, tau,
-               __int_as_float(d.rs[2 * d.m + i]), __int_as_float(d.rs[3 * d.m + i]),
-               __int_as_float(d.cs[2 * d.n + j]), __int_as_float(d.cs[3 * d.n + j]), n_unc, n_rep);
+  if (recon_finish(d, cx, mode, cp, c0, S1, S2, L, rsh, csh, sig, tau,
+                   __int_as_float(d.rs[2 * d.m + i]), __int_as_float(d.rs[3 * d.m + i]),
+                   __int_as_float(d.cs[2 * d.n + j]), __int_as_float(d.cs[3 * d.n + j]), n_unc)) {
+    dot_entry(d, i, j, cp, c0);
+    ++n_rep;
+  }
 }
 
 // Two consecutive rows i0, i0+1 of column j with 8-byte loads of every plane (m even): all
@@ -880,7 +891,13 @@ __device__ __forceinline__ void recon_pair(const ggemm_recon_desc_t& d, const Re
     double* cp = cbase + x;
     const double c0 = (beta == 0.0) ? 0.0 : *cp;
     const int rsh = x ? rsh2.y : rsh2.x, sig = x ? sig2.y : sig2.x;
-    if (recon_special(d, i0 + x, j, cp, c0, rsh, csh, sig, tau, n_saf)) continue;
+    if (const int sp = recon_special(d, cp, c0, rsh, csh, sig, tau)) {
+      if (sp == 2) {
+        dot_entry(d, i0 + x, j, cp, c0);
+        ++n_saf;
+      }
+      continue;
+    }
     int32_t v[kMaxModuli + 1];
 #pragma unroll
     for (int l = 0; l <= kMaxModuli; ++l) v[l] = x ? c2[l].y : c2[l].x;
@@ -891,9 +908,12 @@ __device__ __forceinline__ void recon_pair(const ggemm_recon_desc_t& d, const Re
 #pragma unroll
     for (int l = 0; l <= kMaxModuli; ++l)
       if (l == N) L = v[l];
-    recon_finish(d, cx, mode, i0 + x, j, cp, c0, S1, S2, L, rsh, csh, sig, tau,
-                 __int_as_float(x ? da2.y : da2.x), __int_as_float(x ? na2.y : na2.x), fdb, fnb,
-                 n_unc, n_rep);
+    if (recon_finish(d, cx, mode, cp, c0, S1, S2, L, rsh, csh, sig, tau,
+                     __int_as_float(x ? da2.y : da2.x), __int_as_float(x ? na2.y : na2.x), fdb,
+                     fnb, n_unc)) {
+      dot_entry(d, i0 + x, j, cp, c0);
+      ++n_rep;
+    }
   }
 }
 
@@ -930,9 +950,12 @@ __device__ __forceinline__ void flush_counters(unsigned n_unc, unsigned n_rep, u
 
 // Reconstruct from int32 products: block `local` of the problem takes 1024 consecutive
 // column-major entries, 4 per thread (two pairs when m is even).
-__device__ __forceinline__ void recon_c32_block(const ggemm_recon_desc_t& d, long long local,
-                                                int mode, unsigned& n_unc, unsigned& n_rep,
-                                                unsigned& n_saf) {
+// Not inlined: the digit-layout body then keeps all 128 registers for itself (the int32 body
+// is the rare layout, used only for narrow problems).
+__device__ __noinline__ void recon_c32_block(const ggemm_recon_desc_t* __restrict__ dp,
+                                             long long local, int mode, unsigned& n_unc,
+                                             unsigned& n_rep, unsigned& n_saf) {
+  const ggemm_recon_desc_t d = *dp;
   if (d.N >= 1 && d.N <= kMaxModuli && d.m > 0 && d.n > 0) {
     const ReconCtx cx = recon_ctx(d);
     const long long mn = (long long)d.m * d.n;
@@ -964,87 +987,115 @@ __device__ __forceinline__ void recon_c32_block(const ggemm_recon_desc_t& d, lon
 // takes row 64 b + t / 4 and the 8 columns 8 (t % 4) .. 8 (t % 4) + 7 of the record, so that a
 // warp reads 256 contiguous bytes of each digit plane per load.  The digit and abs-plane loads
 // of a thread (8 bytes per digit plane, 32 bytes of the abs plane) are all issued before its
-// first entry is reconstructed.  Column statistics are staged in shared memory.
-// Every thread of the block calls it.
+// first arithmetic.  The CRT sums run plane by plane over the thread's 8 entries, so each
+// plane's weights are read once per thread instead of once per entry.  Column statistics are
+// staged in shared memory.  Every thread of the block calls it.
 __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long long local,
                                                int mode, unsigned& n_unc, unsigned& n_rep,
                                                unsigned& n_saf) {
-  __shared__ int s_col[4][32];  // csh, tau, ||dB|| bits, ||B'|| bits of the 32 columns
+  __shared__ int s_sh[2][32];      // csh, tau of the 32 columns
+  __shared__ double s_nrm[2][32];  // ||dB_j||, ||B'_j|| (float upper bounds, widened once)
   const bool ok_desc = d.N >= 1 && d.N <= kMaxModuli && d.m > 0 && d.n > 0;
   const long long rblocks = ok_desc ? (d.m + kY8Rows - 1) / kY8Rows : 1;
   const int ch = ok_desc ? (int)(local / rblocks) : 0;
   const int i = (int)(local - ch * rblocks) * kY8Rows + (threadIdx.x >> 2);
   const int cg = threadIdx.x & 3;
   const bool planes = ok_desc && d.alpha != 0.0 && d.k > 0;
-  if (threadIdx.x < 128) {
-    const int st = threadIdx.x >> 5, j = ch * 32 + (threadIdx.x & 31);
-    s_col[st][threadIdx.x & 31] = (ok_desc && d.alpha != 0.0 && j < d.n) ? d.cs[st * d.n + j] : 0;
+  if (threadIdx.x < 64) {
+    const int st = threadIdx.x >> 5, x = threadIdx.x & 31, j = ch * 32 + x;
+    const bool v = ok_desc && d.alpha != 0.0 && j < d.n;
+    s_sh[st][x] = v ? d.cs[st * d.n + j] : 0;
+    s_nrm[st][x] = v ? (double)__int_as_float(d.cs[(2 + st) * d.n + j]) : 0.0;
   }
   __syncthreads();
-  if (ok_desc && i < d.m) {
-    const ReconCtx cx = recon_ctx(d);
-    const int N = cx.N;
-    const int j0 = ch * 32 + cg * 8;
-    const int ncol = min(8, d.n - j0);
-    const long long rec = ((long long)ch * d.m + i) * 32 + cg * 8;
-    const uint8_t* Y = reinterpret_cast<const uint8_t*>(d.C32);
-    uint2 yv[kMaxModuli];
-    int4 l0 = make_int4(0, 0, 0, 0), l1 = l0;
-    int rsh = 0, sig = 0;
-    float fda = 0.f, fna = 0.f;
-    if (planes) {
+  if (!ok_desc || i >= d.m) return;
+  const ReconCtx cx = recon_ctx(d);
+  const int N = cx.N;
+  const int j0 = ch * 32 + cg * 8;
+  const int ncol = min(8, d.n - j0);
+  const long long rec = ((long long)ch * d.m + i) * 32 + cg * 8;
+  const uint8_t* Y = reinterpret_cast<const uint8_t*>(d.C32);
+  uint2 yv[kMaxModuli];
+  int4 l0 = make_int4(0, 0, 0, 0), l1 = l0;
+  if (planes) {
 #pragma unroll
-      for (int l = 0; l < kMaxModuli; ++l)
-        if (l < N) yv[l] = __ldg(reinterpret_cast<const uint2*>(Y + l * d.c_plane + rec));
-      const int4* lp = reinterpret_cast<const int4*>(
-          reinterpret_cast<const int32_t*>(Y + (long long)N * d.c_plane) + rec);
-      l0 = __ldg(lp);
-      l1 = __ldg(lp + 1);
-    }
-    if (d.alpha != 0.0) {
-      rsh = __ldg(d.rs + i);
-      sig = __ldg(d.rs + d.m + i);
-      fda = __int_as_float(__ldg(d.rs + 2 * d.m + i));
-      fna = __int_as_float(__ldg(d.rs + 3 * d.m + i));
-    }
-    double* crow = d.C + i + (long long)j0 * d.ldc;
-    if (d.beta != 0.0)  // the second half's entries of C, fetched while the first is computed
-      for (int x = 4; x < ncol; ++x) prefetch_l2(crow + x * d.ldc);
-    // two halves of 4 entries: the digits of a half are bytes of one 32-bit word per plane
-#pragma unroll 1
-    for (int h = 0; h < 2; ++h) {
-      const int xb = 4 * h;
-      if (xb >= ncol) break;
-      double c0[4];
+    for (int l = 0; l < kMaxModuli; ++l)
+      if (l < N) yv[l] = __ldg(reinterpret_cast<const uint2*>(Y + l * d.c_plane + rec));
+    const int4* lp = reinterpret_cast<const int4*>(
+        reinterpret_cast<const int32_t*>(Y + (long long)N * d.c_plane) + rec);
+    l0 = __ldg(lp);
+    l1 = __ldg(lp + 1);
+  }
+  int rsh = 0, sig = 0;
+  double da = 0.0, na = 0.0;
+  if (d.alpha != 0.0) {
+    rsh = __ldg(d.rs + i);
+    sig = __ldg(d.rs + d.m + i);
+    da = (double)__int_as_float(__ldg(d.rs + 2 * d.m + i));
+    na = (double)__int_as_float(__ldg(d.rs + 3 * d.m + i));
+  }
+  double* crow = d.C + i + (long long)j0 * d.ldc;
+  double c0[4];  // entries of C of the current half (the second half is prefetched to L2)
 #pragma unroll
-      for (int x = 0; x < 4; ++x)
-        c0[x] = (d.beta != 0.0 && xb + x < ncol) ? crow[(xb + x) * d.ldc] : 0.0;
-      uint32_t yw[kMaxModuli];
+  for (int x = 0; x < 4; ++x) c0[x] = (d.beta != 0.0 && x < ncol) ? crow[x * d.ldc] : 0.0;
+  if (d.beta != 0.0)
+    for (int x = 4; x < ncol; ++x) prefetch_l2(crow + x * d.ldc);
+  // CRT sums of the 8 entries, plane by plane
+  uint64_t S1[8];
+  uint32_t S2[8];
 #pragma unroll
-      for (int l = 0; l < kMaxModuli; ++l) yw[l] = h ? yv[l].y : yv[l].x;
-      const int4 lq = h ? l1 : l0;
+  for (int x = 0; x < 8; ++x) {
+    S1[x] = 0;
+    S2[x] = 0;
+  }
+  if (planes) {
 #pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        if (xb + x >= ncol) break;
-        double* cp = crow + (xb + x) * d.ldc;
-        const int cx8 = cg * 8 + xb + x;
-        const int csh = s_col[0][cx8], tau = s_col[1][cx8];
-        if (recon_special(d, i, j0 + xb + x, cp, c0[x], rsh, csh, sig, tau, n_saf)) continue;
-        uint64_t S1 = 0;
-        uint32_t S2 = 0;
+    for (int l = 0; l < kMaxModuli; ++l) {
+      if (l >= N) break;
+      const uint64_t w1 = c_tab.s1[N][l];
+      const uint32_t w2 = c_tab.s2[N][l];
 #pragma unroll
-        for (int l = 0; l < kMaxModuli; ++l) {
-          if (l >= N) break;
-          const uint32_t y = (yw[l] >> (8 * x)) & 255u;
-          S1 += c_tab.s1[N][l] * (uint64_t)y;
-          S2 += c_tab.s2[N][l] * y;
-        }
-        const int32_t L = x == 0 ? lq.x : x == 1 ? lq.y : x == 2 ? lq.z : lq.w;
-        recon_finish(d, cx, mode, i, j0 + xb + x, cp, c0[x], S1, S2, L, rsh, csh, sig, tau, fda,
-                     fna, __int_as_float(s_col[2][cx8]), __int_as_float(s_col[3][cx8]), n_unc,
-                     n_rep);
+      for (int x = 0; x < 8; ++x) {
+        const uint32_t y = __byte_perm(x < 4 ? yv[l].x : yv[l].y, 0u, 0x4440u + (x & 3));
+        S1[x] += w1 * y;
+        S2[x] += w2 * y;
       }
     }
+  }
+  // two halves of four entries (one copy of the finishing code per half position); entries
+  // that need an FP64 dot (safety fallback, repair) are only marked here
+  unsigned need_saf = 0, need_rep = 0;
+#pragma unroll 1
+  for (int h = 0; h < 2; ++h) {
+    const int xb = 4 * h;
+    if (xb >= ncol) break;
+    const int4 lq = h ? l1 : l0;
+    if (h)
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+        c0[x] = (d.beta != 0.0 && 4 + x < ncol) ? crow[(4 + x) * d.ldc] : 0.0;
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+      if (xb + x >= ncol) break;
+      double* cp = crow + (xb + x) * d.ldc;
+      const int cx8 = cg * 8 + xb + x;
+      const int csh = s_sh[0][cx8], tau = s_sh[1][cx8];
+      if (const int sp = recon_special(d, cp, c0[x], rsh, csh, sig, tau)) {
+        need_saf |= (sp == 2 ? 1u : 0u) << (xb + x);
+        continue;
+      }
+      const int32_t L = x == 0 ? lq.x : x == 1 ? lq.y : x == 2 ? lq.z : lq.w;
+      if (recon_finish(d, cx, mode, cp, c0[x], h ? S1[4 + x] : S1[x], h ? S2[4 + x] : S2[x], L,
+                       rsh, csh, sig, tau, da, na, s_nrm[0][cx8], s_nrm[1][cx8], n_unc))
+        need_rep |= 1u << (xb + x);
+    }
+  }
+  n_saf += __popc(need_saf);
+  n_rep += __popc(need_rep);
+  for (unsigned need = need_saf | need_rep; need; need &= need - 1) {
+    const int x = __ffs(need) - 1;
+    double* cp = crow + x * d.ldc;
+    dot_entry(d, i, j0 + x, cp, d.beta != 0.0 ? *cp : 0.0);
   }
 }
 
@@ -1057,7 +1108,7 @@ __global__ void __launch_bounds__(kReconThreads, 2)
   const long long local = (long long)blockIdx.x - prefix[owner];
   unsigned n_unc = 0, n_rep = 0, n_saf = 0;
   if (d.layout == GGEMM_PRODUCTS_DIGITS) recon_y8_block(d, local, mode, n_unc, n_rep, n_saf);
-  else recon_c32_block(d, local, mode, n_unc, n_rep, n_saf);
+  else recon_c32_block(descs + owner, local, mode, n_unc, n_rep, n_saf);
   flush_counters(n_unc, n_rep, n_saf, cnt);
 }
 
