@@ -152,9 +152,9 @@ void make_dev_tables(const CrtTables& t, DevTables* d) {
     d->pf[l] = (float)p;
     d->invpf[l] = 1.0f / (float)p;
     uint32_t w = 1u % p;
-    for (int i = 0; i < kDigits; ++i) {
-      d->w[l][i] = (float)w;
-      for (int b = 0; b < 10; ++b) w = (w << 1) % p;
+    for (int i = 0; i < kByteDigits; ++i) {
+      d->wb[l][i] = (int8_t)(2 * w > p ? (int)w - (int)p : (int)w);
+      w = (w << 8) % p;
     }
     d->p[l] = p;
     d->magic[l] = t.magic[l];

@@ -14,7 +14,7 @@ constexpr int kMaxModuli = 20;
 constexpr int kS2Bits = 18;
 constexpr int kShiftNonfinite = -2147483647 - 1;  // row / column contains NaN or Inf
 constexpr int kShiftZero = -2147483647;           // row / column is all zero (abs shift)
-constexpr int kDigits = 8;                        // 10-bit digits of |trunc(2^s a)| < 2^80
+constexpr int kByteDigits = 12;                   // bytes of trunc(2^s a) as 96-bit integer
 
 // Host tables, field for field the content of the reference's oz2_crt_tables.
 struct CrtTables {
@@ -34,10 +34,10 @@ struct CrtTables {
 
 // What the kernels use.
 struct DevTables {
-  // prep: residues of a 10-bit-digit expansion, evaluated in FP32 (exact, see prep.cuh)
+  // prep: residues of a byte-digit expansion (tensor-core dot, then an FP32 rounding step)
   float pf[kMaxModuli];
   float invpf[kMaxModuli];
-  float w[kMaxModuli][kDigits];  // 2^(10 i) mod p_l
+  int8_t wb[kMaxModuli][kByteDigits];  // 2^(8 i) mod p_l, symmetric representative
   double T[kMaxModuli + 1];
   // reconstruct
   uint32_t p[kMaxModuli];

@@ -1,7 +1,8 @@
 // kernels.cu -- the three sm_100a kernels of the emulated grouped FP64 GEMM:
 //   prep_kernel   FP64 operands -> per-row power-of-two shifts, N int8 residue planes + the
 //                 abs plane, written directly in the tensor-core operand image layout
-//                 (ggemm_stages.h); HBM / integer-ALU bound.
+//                 (ggemm_stages.h); the residues of all planes come from one tcgen05.mma of
+//                 byte digits against block-diagonal weights; HBM bound.
 //   gemm_kernel   persistent tcgen05.mma.kind::i8 GEMM over every (problem, plane, tile):
 //                 bulk copies -> shared-memory ring (mbarriers) -> TMEM int32 accumulators ->
 //                 epilogue warps write CRT digit bytes (or int32 products); tensor-core bound.
@@ -68,96 +69,247 @@ __device__ __forceinline__ int32_t norm_ub_bits(double x) {
 }
 
 // ============================================================================== prep kernel
-// Residues.  For an integer-valued double x with |x| < 2^80, write |x| = sum_i d_i 2^(10 i)
-// (8 ten-bit digits).  For odd p:
-//     t = sum_i (+-d_i) * (2^(10 i) mod p)        |t| <= 8 * 1023 * 254 < 2^21: exact in FP32
-//     s = t - p * rint(t * fl(1/p))               exact symmetric residue of x mod p:
-// |t * fl(1/p) - t/p| <= 2^21/167 * 2^-24 + 2^-11 < 0.00125 while t/p is at least 1/(2p) >=
-// 0.00196 away from any half-integer (p odd), so rint picks round(t/p) and |s| <= (p-1)/2.
-// For p = 256 the residue is the low byte of x (negated for x < 0), read as int8.
+// Residues through the tensor cores.  x = trunc(2^s a) is an integer-valued double with
+// |x| < 2^80.  Read as a 96-bit two's complement integer, its bytes u_i (i < 12) give signed
+// bytes s_i = u_i - 256 c_i with carries c_i = u_i >> 7, and
+//     x = sum_{i<12} s_i 2^(8i) + sum_{i<11} c_i 2^(8(i+1))
+// (the top carry c_11 is the sign bit and cancels the 2^96 of the two's complement).  These 23
+// small integers, plus the abs-plane byte, form a 32-byte int8 "digit slot" per element.  For
+// a modulus p, t = sum_d slot_d W_p[d] with W_p[d] the symmetric residue of the digit's weight
+// (2^(8i) or 2^(8(i+1)) mod p) satisfies t = x (mod p) and |t| <= 12*128*127 + 11*127 < 2^18.
+// One tcgen05.mma (kind::i8, exact int32) computes t for every plane: an MMA row carries the
+// slots of 4 consecutive K positions of one row of the operand (K = 4 x 32 bytes), and the
+// weight matrix is block diagonal, column 4 l + e holding plane l's weights against slot e.
+// The epilogue turns t into the residue byte: with M = 1.5 * 2^23, the float M + t is exact,
+// fma(t, fl(1/p), M) = M + round(t / p) (|t| / p < 2^11, and t / p is at least 1/(2p) away from
+// a half-integer for odd p), and the low byte of bits(M + t) - bits(M + q) p is (t - q p) mod 256
+// because bits(M) = 0x4B400000 is a multiple of 256: the symmetric residue as int8.  For
+// p = 256 the weights reduce t to the low byte of x; the abs plane's weights select its byte.
 // The result is identical to the reference's Barrett / table evaluation
 // (src/ozaki2_numerics.cu:174-205): a residue class has exactly one symmetric representative.
-struct ElemDigits {
-  float f[kDigits];   // signed digits
-  uint32_t low;       // low byte of x (two's complement for x < 0)
-  bool wide;          // |x| >= 2^60: digits 6 and 7 in use
-};
+constexpr int kPrepTileBytes = 4 * 16 * 256;  // 4 slots (K steps) x 16 row groups x 256 B
+constexpr int kPrepMaxCols = 96;              // 4 (N + 1) rounded up to 16, N <= 20
+constexpr int kPrepWBytes = 4 * (kPrepMaxCols / 8) * 256;
 
-__device__ __forceinline__ void split_digits(double xt, ElemDigits& e) {
-  const uint64_t bits = (uint64_t)__double_as_longlong(xt);
-  const bool neg = (bits >> 63) != 0;
-  const int ex = (int)((bits >> 52) & 0x7FF);
-  uint64_t lo = 0, hi = 0;
-  if (ex >= 1023) {  // |x| >= 1 (x is an integer)
-    const uint64_t mant = (bits & 0xFFFFFFFFFFFFFull) | (1ull << 52);
-    const int sh = ex - 1075;  // |x| = mant * 2^sh, -52 <= sh <= 27
-    if (sh <= 0) {
-      lo = mant >> (-sh);
-    } else {
-      lo = mant << sh;
-      hi = mant >> (64 - sh);
-    }
-  }
-  const float sgn = neg ? -1.0f : 1.0f;
-  const float bias = neg ? 8388608.0f : -8388608.0f;
-#pragma unroll
-  for (int i = 0; i < 6; ++i) {
-    const uint32_t d = (uint32_t)(lo >> (10 * i)) & 1023u;
-    e.f[i] = fmaf(__uint_as_float(0x4B000000u | d), sgn, bias);
-  }
-  const uint32_t d6 = (uint32_t)((lo >> 60) | (hi << 4)) & 1023u;
-  const uint32_t d7 = (uint32_t)(hi >> 6) & 1023u;
-  e.f[6] = fmaf(__uint_as_float(0x4B000000u | d6), sgn, bias);
-  e.f[7] = fmaf(__uint_as_float(0x4B000000u | d7), sgn, bias);
-  e.wide = (hi | (lo >> 60)) != 0;
-  const uint32_t lb = (uint32_t)lo & 255u;
-  e.low = neg ? ((0u - lb) & 255u) : lb;
+// A CTA is two independent halves of 4 warps.  Each half owns one tile of 128 MMA rows per
+// round (its own slot buffers, mbarriers and TMEM accumulators) and synchronizes only its own
+// 128 threads (barrier 1 + half), so one half's MMA and memory waits overlap the other's
+// work.  Rounds are pipelined: for N <= 15 the accumulators are double buffered and round i's
+// MMA runs while the half turns round i - 1's accumulators into residue bytes; for N > 15 (wider
+// accumulators) the half finishes round i - 1 first and round i's MMA overlaps the next round's
+// digit slots.
+struct PrepSmem {
+  uint8_t adig[2][2][kPrepTileBytes];  // [half][buffer] digit slots (1024-byte aligned)
+  uint8_t wts[kPrepWBytes];            // block-diagonal weights, K-major, 32-byte swizzle
+  double a[8][32];
+  double b[8][32];
+  double rowmax[32];
+  int sh[32], sg[32];
+  uint64_t bar[2][2];  // [half][buffer]
+  uint32_t tmem;
+  int abort;
+  int issued[2], waited[2];  // per half: rounds whose MMAs were issued / seen complete
+};
+constexpr size_t kPrepSmem = 1024 + sizeof(PrepSmem);
+constexpr int kPrepTmemCols = 256;
+// TMEM column stride of one accumulator: n_cols rounded up to a power of two (>= 32).
+__host__ __device__ constexpr int prep_acc_stride(int n_cols) {
+  return n_cols <= 32 ? 32 : n_cols <= 64 ? 64 : 128;
+}
+// Double-buffered accumulators fit (2 halves x 2 buffers x stride <= 256 columns).
+__device__ __forceinline__ bool prep_dbuf(int n_cols) {
+  return 4 * prep_acc_stride(n_cols) <= kPrepTmemCols;
+}
+// TMEM column of the accumulator of (half, buffer).
+__device__ __forceinline__ uint32_t prep_region(int n_cols, int half, int bf) {
+  return prep_dbuf(n_cols) ? (uint32_t)((2 * half + bf) * prep_acc_stride(n_cols))
+                           : (uint32_t)(half * 128);
+}
+// Barrier of the 128 threads of one half (ids 1 and 2; 0 is __syncthreads).
+__device__ __forceinline__ void half_sync(int half) {
+  if (half) asm volatile("bar.sync 2, 128;" ::: "memory");
+  else asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
-// Symmetric residue of x mod p_l (odd p) as the low byte of a 32-bit word.  The quotient is
-// rounded by adding 1.5 * 2^23 in the same FMA that forms t * fl(1/p): the sum lies in
-// [2^23, 2^24), where the float spacing is 1, so the FMA rounds the exact product to the nearest
-// integer.  That integer is round(t / p) by the bound above (the exact product is even closer to
-// t / p than the rounded one), so all four steps run on the FMA pipe and none is a conversion.
-template <int D>
-__device__ __forceinline__ uint32_t odd_residue_byte(const ElemDigits& e, int l) {
-  float t = e.f[0];
+// Abs-plane value floor(2^sg |a|) in [0, 127] (0 for an all-zero row): min(127, .) commutes
+// with truncation of a non-negative value, so one truncating conversion does both.
+__device__ __forceinline__ uint32_t abs_byte(double a, int sg) {
+  if (sg == kShiftZero) return 0u;
+  return __double2uint_rz(fmin(127.0, mul_pow2(fabs(a), sg)));
+}
+
+// x = trunc(xs) and the three 32-bit words of x as a 96-bit two's complement integer.
+// narrow: |xs| < 2^63 (every N <= 16, as |x| <= T[N] < 2^62.1): one truncating conversion
+// gives x as an int64.  Otherwise (|x| < 2^80) the words come from an exact FP64 split.
+__device__ __forceinline__ void trunc_words(double xs, bool narrow, double& xt, uint32_t& w0,
+                                            uint32_t& w1, uint32_t& w2) {
+  if (narrow) {
+    const long long xi = __double2ll_rz(xs);
+    xt = (double)xi;  // exact: xi came from a double
+    w0 = (uint32_t)xi;
+    w1 = (uint32_t)((unsigned long long)xi >> 32);
+    w2 = (uint32_t)(xi >> 63);
+  } else {
+    xt = trunc(xs);
+    const double xh = floor(xt * 0x1p-32);
+    const double xl = fma(-xh, 0x1p32, xt);  // in [0, 2^32), exact
+    w0 = (uint32_t)__double_as_longlong(xl + 0x1p52);
+    const long long h = __double_as_longlong(xh + 0x1.8p52) - __double_as_longlong(0x1.8p52);
+    w1 = (uint32_t)h;
+    w2 = (uint32_t)((unsigned long long)h >> 32);
+  }
+}
+
+// Digit slot of the words of x and the abs byte ab:
+//   bytes 0..11  s_i (x as 96-bit two's complement), bytes 12..22 c_0..c_10, byte 23 ab.
+__device__ __forceinline__ void digit_slot(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t ab,
+                                           uint4& lo, uint4& hi) {
+  lo = make_uint4(w0, w1, w2, (w0 >> 7) & 0x01010101u);
+  hi = make_uint4((w1 >> 7) & 0x01010101u, ((w2 >> 7) & 0x00010101u) | (ab << 24), 0u, 0u);
+}
+
+// Slot e of MMA row rho of the tile of `half` in buffer bf (K-major image, 32-byte swizzle:
+// slot e is K step e).
+__device__ __forceinline__ void put_slot(PrepSmem& sm, int half, int bf, int rho, int e,
+                                         const uint4& lo, const uint4& hi) {
+  const int rr = rho & 7, sw = (rr >> 2) << 4;
+  uint8_t* base = sm.adig[half][bf] + (e * 16 + (rho >> 3)) * 256 + rr * 32;
+  *reinterpret_cast<uint4*>(base + sw) = lo;
+  *reinterpret_cast<uint4*>(base + (16 ^ sw)) = hi;
+}
+
+// Block-diagonal weights: row n = 4 l + e of the B operand holds plane l's weights in K step
+// (slot) e and zeros elsewhere; planes l > N are zero.
+__device__ void build_weights(PrepSmem& sm, int N, int n_cols) {
+  const int rg = n_cols / 8;
+  for (int c = threadIdx.x; c < 8 * n_cols; c += blockDim.x) {
+    const int half = c & 1, n = (c >> 1) % n_cols, e = (c >> 1) / n_cols;
+    const int l = n >> 2;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if ((n & 3) == e && l <= N) {
 #pragma unroll
-  for (int i = 1; i < D; ++i) t = fmaf(e.f[i], c_tab.w[l][i], t);
-  const float q = fmaf(t, c_tab.invpf[l], 12582912.0f) - 12582912.0f;
-  const float s = fmaf(-q, c_tab.pf[l], t);
-  return __float_as_uint(s + 12582912.0f);  // low byte = s mod 256 (|s| <= 127)
+      for (int b = 0; b < 16; ++b) {
+        const int dd = 16 * half + b;
+        int v = 0;
+        if (l == N) v = dd == 23 ? 1 : 0;
+        else if (dd < 12) v = c_tab.wb[l][dd];
+        else if (dd < 23) v = c_tab.wb[l][dd - 11];
+        w[b >> 2] |= (uint32_t)(v & 255) << (8 * (b & 3));
+      }
+    }
+    const int rr = n & 7;
+    uint8_t* dst = sm.wts + (e * rg + (n >> 3)) * 256 + rr * 32 + ((half ^ (rr >> 2)) << 4);
+    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// Residue byte of t for odd p (low byte of the result; see above).
+__device__ __forceinline__ uint32_t residue_byte(uint32_t t, float invp, uint32_t p) {
+  const uint32_t tm = t + 0x4B400000u;
+  const float r = fmaf(__uint_as_float(tm) - 12582912.0f, invp, 12582912.0f);
+  return tm - __float_as_uint(r) * p;
 }
 
 __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// Residue words of 4 elements for planes 1..N-1, each stored as soon as it is packed
-// (word l goes to dst + l * pb) so that no per-plane array stays live in registers.
-template <int D>
-__device__ __forceinline__ void store_odd_planes4(const ElemDigits (&e)[4], int N, int8_t* dst,
-                                                  long long pb, bool store) {
+// Bounded wait (every thread of a half) for the MMAs of one of its buffers; on a timeout the
+// block gives up.
+__device__ __forceinline__ bool prep_wait(PrepSmem& sm, int half, int bf, uint32_t parity,
+                                          DevCounters* cnt) {
+  if (mbar_try_wait(&sm.bar[half][bf], parity) ||
+      mbar_wait(&sm.bar[half][bf], parity, global_timer_ns() + 4000000000ull, &sm.abort)) {
+    if ((threadIdx.x & 127) == 0) ++sm.waited[half];
+    return true;
+  }
+  sm.abort = 1;
+  atomicCAS(&cnt->status, 0u, (unsigned)kStatusPrepTimeout);
+  return false;
+}
+
+// Second half of round i of this thread's half (its slots are written to buffer i & 1): issues
+// round i's MMAs (thread 0 of the half, committed to bar[half][i & 1]) and turns round i - 1's
+// accumulators into residue bytes (epi(col), col = their TMEM column; when prev).  Returns
+// false once the block has given up.
+template <typename Epi>
+__device__ __forceinline__ bool prep_round(PrepSmem& sm, uint32_t tmem, int n_cols, int i,
+                                           bool prev, Epi&& epi, DevCounters* cnt) {
+  const int half = threadIdx.x >> 7;
+  const bool dbuf = prep_dbuf(n_cols);
+  const int pb = (i - 1) & 1;
+  const uint32_t pp = (uint32_t)((i - 1) >> 1) & 1u;
+  fence_proxy_async_smem();
+  if (!dbuf && prev && prep_wait(sm, half, pb, pp, cnt)) epi(prep_region(n_cols, half, 0));
+  tc_fence_before();
+  half_sync(half);  // slots of round i written; accumulators to be overwritten are read
+  tc_fence_after();
+  if (sm.abort) return false;
+  if ((threadIdx.x & 127) == 0) {
+    const int bf = i & 1;
+    const uint32_t idesc = idesc_i8(128, n_cols);
+    const uint32_t wb = smem_addr(sm.wts);
+    const uint32_t ab = smem_addr(sm.adig[half][bf]);
+    const uint32_t d = tmem + prep_region(n_cols, half, bf);
 #pragma unroll
-  for (int l = 1; l < kMaxModuli; ++l) {
-    if (l >= N) break;
-    const uint32_t w = pack4(odd_residue_byte<D>(e[0], l), odd_residue_byte<D>(e[1], l),
-                             odd_residue_byte<D>(e[2], l), odd_residue_byte<D>(e[3], l));
-    if (store) *reinterpret_cast<uint32_t*>(dst + l * pb) = w;
+    for (int e = 0; e < 4; ++e)
+      mma_i8(d, smem_desc_sw32(ab + e * 16 * 256, 256),
+             smem_desc_sw32(wb + e * (n_cols / 8) * 256, 256), idesc, e > 0 ? 1u : 0u);
+    mma_commit(&sm.bar[half][bf]);
+    ++sm.issued[half];
+  }
+  if (dbuf && prev && prep_wait(sm, half, pb, pp, cnt)) epi(prep_region(n_cols, half, pb));
+  return true;
+}
+
+// Epilogue of a round for one thread (after its MMAs completed), compiled per moduli count N
+// so that every plane index, constant and branch is resolved at compile time: its MMA row
+// (TMEM lane 32 (warp % 4) + lane of the accumulator) holds t for 4 consecutive K positions of
+// one row, column 4 l + e for plane l, element e; it writes one 32-bit word (4 residue bytes)
+// per plane at dst + l * pb.  Groups of 4 planes (16 columns) are loaded from TMEM; the load of
+// group g + 1 overlaps the bytes of group g.
+template <int N>
+__device__ __forceinline__ void prep_epilogue_n(uint32_t taddr, int8_t* dst, long long pb,
+                                                bool store) {
+  constexpr int G = (N + 4) / 4;
+  uint32_t v[2][16];
+  tmem_ld_32x32b_x16(taddr, v[0]);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    tmem_ld_wait(v[g & 1]);
+    if (g + 1 < G) tmem_ld_32x32b_x16(taddr + (uint32_t)((g + 1) * 16), v[(g + 1) & 1]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int l = 4 * g + i;
+      if (l > N) break;
+      uint32_t b[4];
+      if (l == 0 || l == N) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) b[e] = v[g & 1][4 * i + e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          b[e] = residue_byte(v[g & 1][4 * i + e], c_tab.invpf[l], c_tab.p[l]);
+      }
+      if (store) *reinterpret_cast<uint32_t*>(dst + l * pb) = pack4(b[0], b[1], b[2], b[3]);
+    }
   }
 }
 
-// Abs-plane value floor(2^sg |a|) in [0, 127] (0 for an all-zero row).
-__device__ __forceinline__ uint32_t abs_byte(double a, int sg) {
-  if (sg == kShiftZero) return 0u;
-  const double v = fmin(127.0, trunc(mul_pow2(fabs(a), sg)));
-  return (uint32_t)__double_as_longlong(v + 4503599627370496.0) & 255u;
-}
-
-// trunc(2^sh a) (0 for rows / columns containing NaN or Inf).
-__device__ __forceinline__ double scaled_trunc(double a, int sh) {
-  if (sh == kShiftNonfinite) return 0.0;
-  return trunc(mul_pow2(a, sh));
+// Dispatch on N (one copy of the per-N bodies, not inlined into every caller).
+__device__ __noinline__ void prep_epilogue(uint32_t acc, int N, int8_t* dst, long long pb,
+                                           bool store) {
+  tc_fence_after();  // the TMEM reads follow the completion seen on the mbarrier
+  const uint32_t taddr = acc + ((uint32_t)(((threadIdx.x >> 5) & 3) * 32) << 16);
+  switch (N) {
+#define G2_EPI(n) \
+  case n: prep_epilogue_n<n>(taddr, dst, pb, store); break;
+    G2_EPI(1) G2_EPI(2) G2_EPI(3) G2_EPI(4) G2_EPI(5) G2_EPI(6) G2_EPI(7) G2_EPI(8) G2_EPI(9)
+    G2_EPI(10) G2_EPI(11) G2_EPI(12) G2_EPI(13) G2_EPI(14) G2_EPI(15) G2_EPI(16) G2_EPI(17)
+    G2_EPI(18) G2_EPI(19) G2_EPI(20)
+#undef G2_EPI
+    default: break;
+  }
 }
 
 // Image byte offset of (row r, K position q) inside a plane (ggemm_stages.h).
@@ -167,19 +319,16 @@ __device__ __forceinline__ long long img_off(int rg, int r, int q) {
          (qq & 15);
 }
 
-struct PrepShared {
-  double a[8][32];
-  double b[8][32];
-  double rowmax[32];
-  int sh[32], sg[32];
-};
-
 // Rows of a column-major A: 32 rows per block, 8 warps.  Reduction orders (the reference's,
 // src/ozaki2_numerics.cu:263-364): for every row, 8 chains over K positions q = t (mod 8),
 // ascending, for the max / sum of squares and for ||dA||^2, ||A'||^2; chains combined
-// t = 0..7 from 0.0.
+// t = 0..7 from 0.0.  In a round (32 K positions) thread (warp w, lane r) takes the chain
+// positions k0 + w + 8 j, j = 0..3, of row r: they lie in the K quads g = (w / 4) + 2 j, so
+// half w / 4 (chains 4 (w / 4) .. +3) owns the 4 quads of its parity; MMA row 32 j + r of the
+// half's tile holds quad (w / 4) + 2 j of row r, and the epilogue thread (warp w, lane r)
+// owns quad (w / 4) + 2 (w % 4).
 __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters* cnt,
-                                PrepShared& sm) {
+                                PrepSmem& sm, uint32_t tmem, int n_cols) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int rows = d.rows, K = d.k, N = d.N;
   const int r = blk * 32 + lane;
@@ -189,12 +338,14 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
   const double T = c_tab.T[N];
 
   double mx = 0.0, ss = 0.0;
-  if (valid)
+  if (valid) {
+#pragma unroll 16
     for (int q = w; q < K; q += 8) {
       const double a = X[r + q * ld];
       mx = fmax(mx, fabs(a));
       ss = fma(a, a, ss);
     }
+  }
   sm.a[w][lane] = mx;
   __syncthreads();
   if (w == 0) {
@@ -233,45 +384,64 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
   }
   __syncthreads();
   const int sh = sm.sh[lane], sg = sm.sg[lane];
+  const bool finite = sh != kShiftNonfinite;
+  const bool narrow = N <= 16;
   const int ksteps = (K + 31) >> 5;
   const int rg = (rows + 7) >> 3;
   const bool in_image = (r >> 3) < rg;
-  const long long pb = d.plane_bytes;
+  const int half = w >> 2;
+  const int qe = half + 2 * (w & 3);  // K quad of the epilogue thread
 
   double da = 0.0, na = 0.0;  // chain t = w
-  for (int k0 = 0; k0 < ksteps * 32; k0 += 32) {
-    // ||dA||^2, ||A'||^2 chains: q = k0 + w + 8 j (the reference's chain order)
-    if (sh != kShiftNonfinite) {
+  // operands of the next two rounds are in flight while a round is processed
+  double cur[4], nx1[4], nx2[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int q = k0 + w + 8 * j;
-        const double a = (valid && q < K) ? X[r + q * ld] : 0.0;
-        const double xs = mul_pow2(a, sh);
-        const double xt = trunc(xs);
+  for (int j = 0; j < 4; ++j) {
+    const int q = w + 8 * j;
+    cur[j] = (valid && q < K) ? X[r + q * ld] : 0.0;
+    nx1[j] = (valid && q + 32 < K) ? X[r + (q + 32) * ld] : 0.0;
+  }
+  int i = 0;
+  for (; i < ksteps; ++i) {
+    const int k0 = 32 * i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int q = k0 + 64 + w + 8 * j;
+      nx2[j] = (valid && q < K) ? X[r + q * ld] : 0.0;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w0 = 0u, w1 = 0u, w2 = 0u, ab = 0u;
+      if (finite) {
+        const double xs = mul_pow2(cur[j], sh);
+        double xt;
+        trunc_words(xs, narrow, xt, w0, w1, w2);
         const double fr = xs - xt;
         da = fma(fr, fr, da);
         na = fma(xt, xt, na);
+        ab = abs_byte(cur[j], sg);
       }
+      uint4 lo, hi;
+      digit_slot(w0, w1, w2, ab, lo, hi);
+      put_slot(sm, half, i & 1, 32 * j + lane, w & 3, lo, hi);
     }
-    // residues of the 4 consecutive K positions q0 .. q0+3 (4 bytes per plane)
-    const int q0 = k0 + 4 * w;
-    ElemDigits e[4];
-    uint32_t ab[4];
-    bool wide = false;
+    int8_t* prev_dst = d.img + img_off(rg, r, k0 - 32 + 4 * qe);
+    if (!prep_round(sm, tmem, n_cols, i, i > 0,
+                    [&](uint32_t col) {
+                      prep_epilogue(tmem + col, N, prev_dst, d.plane_bytes, in_image);
+                    },
+                    cnt))
+      break;
 #pragma unroll
-    for (int x = 0; x < 4; ++x) {
-      const int q = q0 + x;
-      const double a = (valid && q < K) ? X[r + q * ld] : 0.0;
-      split_digits(scaled_trunc(a, sh), e[x]);
-      ab[x] = (sh == kShiftNonfinite) ? 0u : abs_byte(a, sg);
-      wide |= e[x].wide;
+    for (int j = 0; j < 4; ++j) {
+      cur[j] = nx1[j];
+      nx1[j] = nx2[j];
     }
-    int8_t* dst = d.img + img_off(rg, r, q0);
-    if (in_image) *reinterpret_cast<uint32_t*>(dst) = pack4(e[0].low, e[1].low, e[2].low, e[3].low);
-    if (__any_sync(0xFFFFFFFFu, wide)) store_odd_planes4<8>(e, N, dst, pb, in_image);
-    else store_odd_planes4<6>(e, N, dst, pb, in_image);
-    if (in_image) *reinterpret_cast<uint32_t*>(dst + N * pb) = pack4(ab[0], ab[1], ab[2], ab[3]);
   }
+  if (i == ksteps && ksteps > 0 &&
+      prep_wait(sm, half, (i - 1) & 1, (uint32_t)((i - 1) >> 1) & 1u, cnt))
+    prep_epilogue(tmem + prep_region(n_cols, half, prep_dbuf(n_cols) ? (i - 1) & 1 : 0), N,
+                  d.img + img_off(rg, r, 32 * (i - 1) + 4 * qe), d.plane_bytes, in_image);
   __syncthreads();
   sm.a[w][lane] = da;
   sm.b[w][lane] = na;
@@ -291,8 +461,11 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
 // Columns of a column-major B: one warp per column, 8 columns (one image row group) per
 // block.  Reduction orders (src/ozaki2_numerics.cu:368-441): max / sum of squares over lane
 // chains q = lane (mod 32); norms over lane chains q = 4 lane + 128 c + e; both combined by the
-// xor butterfly.
-__device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters* cnt) {
+// xor butterfly.  In a round (128 K positions) lane L of warp w takes positions c0 + 4 L + e,
+// e = 0..3, of its column: its own MMA row (32 (w % 4) + L of tile w / 4), so the same thread
+// writes the slots and reads back the residues.
+__device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters* cnt,
+                                PrepSmem& sm, uint32_t tmem, int n_cols) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int rows = d.rows, K = d.k, N = d.N;
   const int col = blk * 8 + w;
@@ -301,12 +474,14 @@ __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters
   const double T = c_tab.T[N];
 
   double mx = 0.0, ss = 0.0;
-  if (valid)
+  if (valid) {
+#pragma unroll 16
     for (int q = lane; q < K; q += 32) {
       const double a = b[q];
       mx = fmax(mx, fabs(a));
       ss = fma(a, a, ss);
     }
+  }
 #pragma unroll
   for (int o = 16; o; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
   const bool resc = valid && needs_rescale(mx);
@@ -327,38 +502,61 @@ __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters
     d.ws[rows + col] = sg;
     if (sh == kShiftNonfinite) atomicAdd(&cnt->nonfinite, 1ull);
   }
+  const bool finite = sh != kShiftNonfinite;
+  const bool narrow = N <= 16;
   const int ksteps = (K + 31) >> 5;
   const int rg = (rows + 7) >> 3;
-  const long long pb = d.plane_bytes;
 
   double da = 0.0, na = 0.0;
-  for (int c0 = 0; c0 < ksteps * 32; c0 += 128) {
-    const int q0 = c0 + 4 * lane;
-    const bool in_k = (q0 >> 5) < ksteps;
-    ElemDigits e[4];
-    uint32_t ab[4];
-    bool wide = false;
+  const int rounds = (ksteps + 3) >> 2;  // 128 K positions per round
+  double cur[4], nx1[4], nx2[4];
 #pragma unroll
-    for (int x = 0; x < 4; ++x) {
-      const int q = q0 + x;
-      const double a = (valid && q < K) ? b[q] : 0.0;
-      double xt = 0.0;
-      if (sh != kShiftNonfinite && in_k) {
-        const double xs = mul_pow2(a, sh);
-        xt = trunc(xs);
+  for (int e = 0; e < 4; ++e) {
+    const int q = 4 * lane + e;
+    cur[e] = (valid && q < K) ? b[q] : 0.0;
+    nx1[e] = (valid && q + 128 < K) ? b[q + 128] : 0.0;
+  }
+  int i = 0;
+  for (; i < rounds; ++i) {
+    const int q0 = 128 * i + 4 * lane;
+    const bool in_k = (q0 >> 5) < ksteps;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) nx2[e] = (valid && q0 + 256 + e < K) ? b[q0 + 256 + e] : 0.0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      uint32_t w0 = 0u, w1 = 0u, w2 = 0u, ab = 0u;
+      if (finite && in_k) {
+        const double xs = mul_pow2(cur[e], sh);
+        double xt;
+        trunc_words(xs, narrow, xt, w0, w1, w2);
         const double fr = xs - xt;
         da = fma(fr, fr, da);
         na = fma(xt, xt, na);
+        ab = abs_byte(cur[e], sg);
       }
-      split_digits(xt, e[x]);
-      ab[x] = (sh == kShiftNonfinite) ? 0u : abs_byte(a, sg);
-      wide |= e[x].wide;
+      uint4 lo, hi;
+      digit_slot(w0, w1, w2, ab, lo, hi);
+      put_slot(sm, w >> 2, i & 1, 32 * (w & 3) + lane, e, lo, hi);
     }
-    int8_t* dst = d.img + img_off(rg, col, in_k ? q0 : 0);
-    if (in_k) *reinterpret_cast<uint32_t*>(dst) = pack4(e[0].low, e[1].low, e[2].low, e[3].low);
-    if (__any_sync(0xFFFFFFFFu, wide)) store_odd_planes4<8>(e, N, dst, pb, in_k);
-    else store_odd_planes4<6>(e, N, dst, pb, in_k);
-    if (in_k) *reinterpret_cast<uint32_t*>(dst + N * pb) = pack4(ab[0], ab[1], ab[2], ab[3]);
+    const int qp = q0 - 128;
+    const bool in_kp = qp >= 0 && (qp >> 5) < ksteps;
+    int8_t* prev_dst = d.img + img_off(rg, col, in_kp ? qp : 0);
+    if (!prep_round(sm, tmem, n_cols, i, i > 0,
+                    [&](uint32_t c) { prep_epilogue(tmem + c, N, prev_dst, d.plane_bytes, in_kp); },
+                    cnt))
+      break;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      cur[e] = nx1[e];
+      nx1[e] = nx2[e];
+    }
+  }
+  if (i == rounds && rounds > 0 &&
+      prep_wait(sm, w >> 2, (i - 1) & 1, (uint32_t)((i - 1) >> 1) & 1u, cnt)) {
+    const int qp = 128 * (i - 1) + 4 * lane;
+    const bool in_kp = (qp >> 5) < ksteps;
+    prep_epilogue(tmem + prep_region(n_cols, w >> 2, prep_dbuf(n_cols) ? (i - 1) & 1 : 0), N,
+                  d.img + img_off(rg, col, in_kp ? qp : 0), d.plane_bytes, in_kp);
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
@@ -382,16 +580,52 @@ __device__ __forceinline__ int find_owner(const P* __restrict__ prefix, int num,
   return lo;
 }
 
-__global__ void __launch_bounds__(kPrepThreads, 2) prep_kernel(const ggemm_prep_desc_t* __restrict__ descs,
-                                                            const int* __restrict__ prefix,
-                                                            int num, DevCounters* cnt) {
-  __shared__ PrepShared sm;
+__global__ void __launch_bounds__(kPrepThreads, 2)
+    prep_kernel(const ggemm_prep_desc_t* __restrict__ descs, const int* __restrict__ prefix,
+                int num, DevCounters* cnt) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  PrepSmem& sm = *reinterpret_cast<PrepSmem*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int owner = find_owner(prefix, num, (int)blockIdx.x);
   const ggemm_prep_desc_t d = descs[owner];
   if (d.N < 1 || d.N > kMaxModuli || d.rows <= 0) return;
+  const int n_cols = (4 * (d.N + 1) + 15) / 16 * 16;
+  build_weights(sm, d.N, n_cols);
+  if (threadIdx.x == 0) {
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&sm.bar[h][0], 1);
+      mbar_init(&sm.bar[h][1], 1);
+      sm.issued[h] = 0;
+      sm.waited[h] = 0;
+    }
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (threadIdx.x < 32) {
+    tmem_alloc(&sm.tmem, kPrepTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem;
   const int blk = (int)blockIdx.x - prefix[owner];
-  if (d.kind == 0) prep_rows_block(d, blk, cnt, sm);
-  else prep_cols_block(d, blk, cnt);
+  if (d.kind == 0) prep_rows_block(d, blk, cnt, sm, tmem, n_cols);
+  else prep_cols_block(d, blk, cnt, sm, tmem, n_cols);
+  // a half that gave up may still have MMAs in flight (at most its last two rounds, since
+  // every round waits for the one before): let them finish (bounded) first
+  __syncthreads();
+  if ((threadIdx.x & 127) == 0) {
+    const int h = threadIdx.x >> 7;
+    int dummy = 0;
+    for (int j = max(sm.waited[h], sm.issued[h] - 2); j < sm.issued[h]; ++j)
+      if (!mbar_wait(&sm.bar[h][j & 1], (uint32_t)(j >> 1) & 1u,
+                     global_timer_ns() + 4000000000ull, &dummy))
+        break;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x < 32) tmem_dealloc(tmem, kPrepTmemCols);
 }
 
 // ============================================================================== GEMM kernel
@@ -1137,6 +1371,9 @@ int upload_tables_current_device() {
   if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kGemmSmem) != cudaSuccess)
     return 3;
+  if (cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kPrepSmem) != cudaSuccess)
+    return 3;
   g_gemm_attr[dev] = true;
   if (cudaDeviceSynchronize() != cudaSuccess) return 4;
   g_uploaded |= 1ull << dev;
@@ -1154,7 +1391,7 @@ int current_device_sms() {
 int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, int num, int total_blocks,
                 DevCounters* cnt, cudaStream_t s) {
   if (num <= 0 || total_blocks <= 0) return 0;
-  prep_kernel<<<total_blocks, kPrepThreads, 0, s>>>(d_descs, d_prefix, num, cnt);
+  prep_kernel<<<total_blocks, kPrepThreads, kPrepSmem, s>>>(d_descs, d_prefix, num, cnt);
   return (int)cudaGetLastError();
 }
 

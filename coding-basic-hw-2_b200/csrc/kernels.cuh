@@ -22,6 +22,7 @@ static_assert(sizeof(DevCounters) == 64, "counter block layout");
 enum : unsigned int {
   kStatusOk = 0,
   kStatusGemmTimeout = 1,  // a residue-GEMM pipeline wait ran past its deadline
+  kStatusPrepTimeout = 2,  // a prep residue-MMA wait ran past its deadline
 };
 
 // Digit layout ("Y8", GGEMM_PRODUCTS_DIGITS in ggemm_stages.h) of the products handed from the
