@@ -100,10 +100,19 @@ class Group:
         for m, n, k, alpha, beta in self.shapes:
             kp = (k + 31) // 32 * 32
             prep += 8.0 * (m * k + k * n) + (N + 1) * (m + n) * kp + 16.0 * (m + n)
-            recon += 4.0 * (N + 1) * m * n + (8.0 * m * n if beta != 0 else 0) + 8.0 * m * n \
+            # products read by the reconstruct: N digit bytes + the int32 abs product per entry
+            # (digit layout), or N + 1 int32 products (int32 layout, narrow problems)
+            per_entry = (N + 4.0) if digit_layout(m, n, N) else 4.0 * (N + 1)
+            recon += per_entry * m * n + (8.0 * m * n if beta != 0 else 0) + 8.0 * m * n \
                 + 16.0 * (m + n)
             ops += 2.0 * m * n * kp * (N + 1)
         return prep, ops, recon
+
+
+def digit_layout(m: int, n: int, N: int) -> bool:
+    """The library's per-problem product layout choice (digit layout unless it is larger)."""
+    plane = ((n + 31) // 32 * m * 32 + 255) // 256 * 256
+    return (N + 4) * plane <= 4 * (N + 1) * ((m * n + 63) // 64 * 64)
 
 
 # ------------------------------------------------------------------------------ helpers
