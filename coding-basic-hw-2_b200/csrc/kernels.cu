@@ -39,6 +39,15 @@ __device__ __forceinline__ double mul_pow2(double x, int e) {
   return x;
 }
 
+// max(m, |a|) on the bit patterns: non-negative doubles order like their unsigned bits, so
+// for finite and infinite |a| this is fmax(m, |a|).  A NaN element wins instead of being skipped;
+// every row / column with a NaN ends with the non-finite shift either way (its sum of squares
+// is NaN), so the shifts, the abs shifts and everything after are unchanged.  (FP64 fmax costs
+// several instructions for its NaN rules.)
+__device__ __forceinline__ unsigned long long absmax_bits(unsigned long long m, double a) {
+  return max(m, (unsigned long long)__double_as_longlong(a) & 0x7FFFFFFFFFFFFFFFull);
+}
+
 __device__ __forceinline__ bool needs_rescale(double maxabs) {
   return maxabs > 0.0 && (maxabs > 0x1p400 || maxabs < 0x1p-400);
 }
@@ -131,11 +140,12 @@ __device__ __forceinline__ void half_sync(int half) {
   else asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
-// Abs-plane value floor(2^sg |a|) in [0, 127] (0 for an all-zero row): min(127, .) commutes
-// with truncation of a non-negative value, so one truncating conversion does both.
+// Abs-plane value floor(2^sg |a|) in [0, 127] (0 for an all-zero row).  2^sg |a| < 128 for
+// every element of a finite row (sg puts the row maximum in [64, 128)), so the truncating
+// conversion is exact; the reference's clamp at 127 is kept as an integer min.
 __device__ __forceinline__ uint32_t abs_byte(double a, int sg) {
   if (sg == kShiftZero) return 0u;
-  return __double2uint_rz(fmin(127.0, mul_pow2(fabs(a), sg)));
+  return min(__double2uint_rz(mul_pow2(fabs(a), sg)), 127u);
 }
 
 // x = trunc(xs) and the three 32-bit words of x as a 96-bit two's complement integer.
@@ -337,22 +347,23 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
   const long long ld = d.ld;
   const double T = c_tab.T[N];
 
-  double mx = 0.0, ss = 0.0;
+  unsigned long long mxb = 0;
+  double ss = 0.0;
   if (valid) {
 #pragma unroll 16
     for (int q = w; q < K; q += 8) {
       const double a = X[r + q * ld];
-      mx = fmax(mx, fabs(a));
+      mxb = absmax_bits(mxb, a);
       ss = fma(a, a, ss);
     }
   }
-  sm.a[w][lane] = mx;
+  sm.a[w][lane] = __longlong_as_double((long long)mxb);
   __syncthreads();
   if (w == 0) {
-    double M = 0.0;
+    unsigned long long M = 0;
 #pragma unroll
-    for (int t = 0; t < 8; ++t) M = fmax(M, sm.a[t][lane]);
-    sm.rowmax[lane] = M;
+    for (int t = 0; t < 8; ++t) M = absmax_bits(M, sm.a[t][lane]);
+    sm.rowmax[lane] = __longlong_as_double((long long)M);
   }
   __syncthreads();
   const double rowmax = sm.rowmax[lane];
@@ -473,17 +484,20 @@ __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters
   const double* __restrict__ b = d.X + (long long)(valid ? col : 0) * d.ld;
   const double T = c_tab.T[N];
 
-  double mx = 0.0, ss = 0.0;
+  unsigned long long mxb = 0;
+  double ss = 0.0;
   if (valid) {
 #pragma unroll 16
     for (int q = lane; q < K; q += 32) {
       const double a = b[q];
-      mx = fmax(mx, fabs(a));
+      mxb = absmax_bits(mxb, a);
       ss = fma(a, a, ss);
     }
   }
 #pragma unroll
-  for (int o = 16; o; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+  for (int o = 16; o; o >>= 1)
+    mxb = max(mxb, (unsigned long long)__shfl_xor_sync(0xFFFFFFFFu, (long long)mxb, o));
+  const double mx = __longlong_as_double((long long)mxb);
   const bool resc = valid && needs_rescale(mx);
   if (resc) {
     const int e = -ilogb(mx);
@@ -1014,7 +1028,7 @@ __device__ __forceinline__ bool recon_finish(const ggemm_recon_desc_t& d, const 
   const int esc = cx.lu1 - rsh - csh;
   const double v = mul_pow2(xr, esc);
   const double emu = (beta == 0.0) ? alpha * v : fma(alpha, v, beta * c0);
-  if (mode == GGEMM_STAGE_REPAIR_OFF || (beta != 0.0 && !isfinite(c0))) {
+  if (mode == GGEMM_STAGE_REPAIR_OFF || (beta != 0.0 && !(fabs(c0) < INFINITY))) {
     *cp = emu;
     return false;
   }
@@ -1023,12 +1037,16 @@ __device__ __forceinline__ bool recon_finish(const ggemm_recon_desc_t& d, const 
   const double Eu = fma(4.0 * u, fabs(xr), fma(et, cx.inv_u1, cx.crt_u)) * (1.0 + 0x1p-40);
   const double E = mul_pow2(Eu, esc);
   double lab = mul_pow2((double)L32, -(sig + tau));
-  lab = fmax(lab, fabs(v) - E) * (1.0 - 0x1p-40);
+  // fmax(lab, |v| - E): lab is never NaN, and a NaN difference keeps lab, as fmax does; the
+  // sign of a zero result is erased below
+  const double dv = fabs(v) - E;
+  lab = (dv > lab ? dv : lab) * (1.0 - 0x1p-40);
   if (lab < 0x1p-1000) lab = 0.0;
   const double aalpha = fabs(alpha);
   const double lhs = aalpha * E * (1.0 + 0x1p-40);
   const double rhs = cx.gam * fma(aalpha, lab, fabs(beta * c0)) * (1.0 - 0x1p-40);
-  const bool cert = cx.gam > 0.0 && E >= 0x1p-1000 && isfinite(lhs) && isfinite(v) && lhs <= rhs;
+  const bool cert = cx.gam > 0.0 && E >= 0x1p-1000 && fabs(lhs) < INFINITY &&
+                    fabs(v) < INFINITY && lhs <= rhs;
   if (cert || mode == GGEMM_STAGE_REPAIR_COUNT) {
     *cp = emu;
     n_unc += cert ? 0u : 1u;
