@@ -319,8 +319,6 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         d.img = h->imgA + h->ua_img[ua];
         d.plane_bytes = (long long)align_up(ggemm_img_plane_bytes(p.m, p.k), kAlign);
         d.ws = h->wsA + h->ua_ws[ua];
-        pp[q] = blocks;
-        blocks += prep_blocks(d);
         ++q;
       }
       if (h->ub_chunk[ub] == -2 - cid) {
@@ -336,10 +334,21 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         d.img = h->imgB + h->ub_img[ub];
         d.plane_bytes = (long long)align_up(ggemm_img_plane_bytes(p.n, p.k), kAlign);
         d.ws = h->wsB + h->ub_ws[ub];
-        pp[q] = blocks;
-        blocks += prep_blocks(d);
         ++q;
       }
+    }
+    // descriptors with N <= 15 first: prep is compiled once per case (launch_prep)
+    std::stable_partition(pd, pd + q,
+                          [](const ggemm_prep_desc_t& d) { return !prep_needs_bias(d.N); });
+    ch.num_prep_lo = 0;
+    ch.prep_blocks_lo = 0;
+    for (int x = 0; x < q; ++x) {
+      pp[x] = blocks;
+      if (!prep_needs_bias(pd[x].N)) {
+        ++ch.num_prep_lo;
+        ch.prep_blocks_lo = blocks + prep_blocks(pd[x]);
+      }
+      blocks += prep_blocks(pd[x]);
     }
     pp[q] = blocks;
     ch.prep_blocks = blocks;
@@ -509,9 +518,9 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
     if (ch.prep_blocks > 0) {
       if (launch_prep(reinterpret_cast<const ggemm_prep_desc_t*>(db + ch.off_prep),
                       reinterpret_cast<const int*>(db + ch.off_prep_prefix), ch.num_prep,
-                      ch.prep_blocks, h->counters, s))
+                      ch.num_prep_lo, ch.prep_blocks_lo, ch.prep_blocks, h->counters, s,
+                      launches))
         return GGEMM_ERR_NUMERICS;
-      ++*launches;
     }
     if (!mark(1)) return GGEMM_ERR_CUDA;
     const GemmJob* jobs = reinterpret_cast<const GemmJob*>(db + ch.off_jobs);

@@ -125,14 +125,13 @@ constexpr int kPrepTmemCols = 256;
 __host__ __device__ constexpr int prep_acc_stride(int n_cols) {
   return n_cols <= 32 ? 32 : n_cols <= 64 ? 64 : 128;
 }
-// Double-buffered accumulators fit (2 halves x 2 buffers x stride <= 256 columns).
-__device__ __forceinline__ bool prep_dbuf(int n_cols) {
-  return 4 * prep_acc_stride(n_cols) <= kPrepTmemCols;
-}
+// Double-buffered accumulators fit (2 halves x 2 buffers x stride <= 256 columns) exactly
+// for N <= 15; above, each half has one accumulator of stride 128 (kBias below: the kernel is
+// compiled once per case).
 // TMEM column of the accumulator of (half, buffer).
+template <bool kBias>
 __device__ __forceinline__ uint32_t prep_region(int n_cols, int half, int bf) {
-  return prep_dbuf(n_cols) ? (uint32_t)((2 * half + bf) * prep_acc_stride(n_cols))
-                           : (uint32_t)(half * 128);
+  return kBias ? (uint32_t)(half * 128) : (uint32_t)((2 * half + bf) * prep_acc_stride(n_cols));
 }
 // Barrier of the 128 threads of one half (ids 1 and 2; 0 is __syncthreads).
 __device__ __forceinline__ void half_sync(int half) {
@@ -213,11 +212,24 @@ __device__ void build_weights(PrepSmem& sm, int N, int n_cols) {
   }
 }
 
-// Residue byte of t for odd p (low byte of the result; see above).
-__device__ __forceinline__ uint32_t residue_byte(uint32_t t, float invp, uint32_t p) {
-  const uint32_t tm = t + 0x4B400000u;
+// With single-buffered accumulators (N > 15) they start from kPrepBias = bits(1.5 * 2^23)
+// instead of zero, so the MMA yields tm = bits(M + t) directly (|t| < 2^22) and the epilogue
+// saves one integer add per residue; the low byte of tm is t's low byte (the bias is a multiple
+// of 256), which the p = 256 plane and the abs plane keep as they are.  With double-buffered
+// accumulators (N <= 15) the refill of one accumulator while the MMA writes the other cost more
+// than it saved (measured), so they start from zero and the epilogue adds the bias.
+constexpr uint32_t kPrepBias = 0x4B400000u;
+
+// Residue byte of t for odd p from tm = kPrepBias + t (low byte of the result; see above).
+__device__ __forceinline__ uint32_t residue_byte(uint32_t tm, float invp, uint32_t p) {
   const float r = fmaf(__uint_as_float(tm) - 12582912.0f, invp, 12582912.0f);
   return tm - __float_as_uint(r) * p;
+}
+
+// Sets the n_cols columns of this thread's lane of the accumulator at `acc` to kPrepBias.
+__device__ __forceinline__ void prep_bias_acc(uint32_t acc, int n_cols) {
+  const uint32_t taddr = acc + ((uint32_t)(((threadIdx.x >> 5) & 3) * 32) << 16);
+  for (int c = 0; c < n_cols; c += 16) tmem_fill_32x32b_x16(taddr + (uint32_t)c, kPrepBias);
 }
 
 __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -242,15 +254,19 @@ __device__ __forceinline__ bool prep_wait(PrepSmem& sm, int half, int bf, uint32
 // round i's MMAs (thread 0 of the half, committed to bar[half][i & 1]) and turns round i - 1's
 // accumulators into residue bytes (epi(col), col = their TMEM column; when prev).  Returns
 // false once the block has given up.
-template <typename Epi>
+template <bool kBias, typename Epi>
 __device__ __forceinline__ bool prep_round(PrepSmem& sm, uint32_t tmem, int n_cols, int i,
                                            bool prev, Epi&& epi, DevCounters* cnt) {
   const int half = threadIdx.x >> 7;
-  const bool dbuf = prep_dbuf(n_cols);
+  constexpr bool dbuf = !kBias;
   const int pb = (i - 1) & 1;
   const uint32_t pp = (uint32_t)((i - 1) >> 1) & 1u;
   fence_proxy_async_smem();
-  if (!dbuf && prev && prep_wait(sm, half, pb, pp, cnt)) epi(prep_region(n_cols, half, 0));
+  if (!dbuf && prev && prep_wait(sm, half, pb, pp, cnt)) {
+    epi(prep_region<kBias>(n_cols, half, 0));
+    prep_bias_acc(tmem + prep_region<kBias>(n_cols, half, 0), n_cols);
+  }
+  if (!dbuf) tmem_st_wait();  // this thread's accumulator reset precedes the MMAs
   tc_fence_before();
   half_sync(half);  // slots of round i written; accumulators to be overwritten are read
   tc_fence_after();
@@ -260,24 +276,28 @@ __device__ __forceinline__ bool prep_round(PrepSmem& sm, uint32_t tmem, int n_co
     const uint32_t idesc = idesc_i8(128, n_cols);
     const uint32_t wb = smem_addr(sm.wts);
     const uint32_t ab = smem_addr(sm.adig[half][bf]);
-    const uint32_t d = tmem + prep_region(n_cols, half, bf);
+    const uint32_t d = tmem + prep_region<kBias>(n_cols, half, bf);
+    const uint32_t acc0 = dbuf ? 0u : 1u;  // biased accumulators add to their start value
 #pragma unroll
     for (int e = 0; e < 4; ++e)
       mma_i8(d, smem_desc_sw32(ab + e * 16 * 256, 256),
-             smem_desc_sw32(wb + e * (n_cols / 8) * 256, 256), idesc, e > 0 ? 1u : 0u);
+             smem_desc_sw32(wb + e * (n_cols / 8) * 256, 256), idesc, e > 0 ? 1u : acc0);
     mma_commit(&sm.bar[half][bf]);
     ++sm.issued[half];
   }
-  if (dbuf && prev && prep_wait(sm, half, pb, pp, cnt)) epi(prep_region(n_cols, half, pb));
+  if (dbuf && prev && prep_wait(sm, half, pb, pp, cnt)) epi(prep_region<kBias>(n_cols, half, pb));
   return true;
 }
 
 // Epilogue of a round for one thread (after its MMAs completed), compiled per moduli count N
 // so that every plane index, constant and branch is resolved at compile time: its MMA row
 // (TMEM lane 32 (warp % 4) + lane of the accumulator) holds t for 4 consecutive K positions of
-// one row, column 4 l + e for plane l, element e; it writes one 32-bit word (4 residue bytes)
-// per plane at dst + l * pb.  Groups of 4 planes (16 columns) are loaded from TMEM; the load of
-// group g + 1 overlaps the bytes of group g.
+// one row, column 4 l + e for plane l, element e (t, or kPrepBias + t when prep_needs_bias(N)); it
+// writes one 32-bit word
+// (4 residue bytes) per plane at dst + l * pb.  Groups of 4 planes (16 columns) are loaded from
+// TMEM; the load of group g + 1 overlaps the bytes of group g.  (The caller resets the
+// accumulator to the bias afterwards; doing it here, in a function that is not inlined, would
+// cost the caller registers.)
 template <int N>
 __device__ __forceinline__ void prep_epilogue_n(uint32_t taddr, int8_t* dst, long long pb,
                                                 bool store) {
@@ -299,11 +319,13 @@ __device__ __forceinline__ void prep_epilogue_n(uint32_t taddr, int8_t* dst, lon
       } else {
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          b[e] = residue_byte(v[g & 1][4 * i + e], c_tab.invpf[l], c_tab.p[l]);
+          b[e] = residue_byte(v[g & 1][4 * i + e] + (prep_needs_bias(N) ? 0u : kPrepBias),
+                              c_tab.invpf[l], c_tab.p[l]);
       }
       if (store) *reinterpret_cast<uint32_t*>(dst + l * pb) = pack4(b[0], b[1], b[2], b[3]);
     }
   }
+
 }
 
 // Dispatch on N (one copy of the per-N bodies, not inlined into every caller).
@@ -337,6 +359,7 @@ __device__ __forceinline__ long long img_off(int rg, int r, int q) {
 // half w / 4 (chains 4 (w / 4) .. +3) owns the 4 quads of its parity; MMA row 32 j + r of the
 // half's tile holds quad (w / 4) + 2 j of row r, and the epilogue thread (warp w, lane r)
 // owns quad (w / 4) + 2 (w % 4).
+template <bool kBias>
 __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters* cnt,
                                 PrepSmem& sm, uint32_t tmem, int n_cols) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -437,7 +460,7 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
       put_slot(sm, half, i & 1, 32 * j + lane, w & 3, lo, hi);
     }
     int8_t* prev_dst = d.img + img_off(rg, r, k0 - 32 + 4 * qe);
-    if (!prep_round(sm, tmem, n_cols, i, i > 0,
+    if (!prep_round<kBias>(sm, tmem, n_cols, i, i > 0,
                     [&](uint32_t col) {
                       prep_epilogue(tmem + col, N, prev_dst, d.plane_bytes, in_image);
                     },
@@ -451,7 +474,7 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
   }
   if (i == ksteps && ksteps > 0 &&
       prep_wait(sm, half, (i - 1) & 1, (uint32_t)((i - 1) >> 1) & 1u, cnt))
-    prep_epilogue(tmem + prep_region(n_cols, half, prep_dbuf(n_cols) ? (i - 1) & 1 : 0), N,
+    prep_epilogue(tmem + prep_region<kBias>(n_cols, half, kBias ? 0 : (i - 1) & 1), N,
                   d.img + img_off(rg, r, 32 * (i - 1) + 4 * qe), d.plane_bytes, in_image);
   __syncthreads();
   sm.a[w][lane] = da;
@@ -475,6 +498,7 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
 // xor butterfly.  In a round (128 K positions) lane L of warp w takes positions c0 + 4 L + e,
 // e = 0..3, of its column: its own MMA row (32 (w % 4) + L of tile w / 4), so the same thread
 // writes the slots and reads back the residues.
+template <bool kBias>
 __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters* cnt,
                                 PrepSmem& sm, uint32_t tmem, int n_cols) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -555,7 +579,7 @@ __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters
     const int qp = q0 - 128;
     const bool in_kp = qp >= 0 && (qp >> 5) < ksteps;
     int8_t* prev_dst = d.img + img_off(rg, col, in_kp ? qp : 0);
-    if (!prep_round(sm, tmem, n_cols, i, i > 0,
+    if (!prep_round<kBias>(sm, tmem, n_cols, i, i > 0,
                     [&](uint32_t c) { prep_epilogue(tmem + c, N, prev_dst, d.plane_bytes, in_kp); },
                     cnt))
       break;
@@ -569,7 +593,7 @@ __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters
       prep_wait(sm, w >> 2, (i - 1) & 1, (uint32_t)((i - 1) >> 1) & 1u, cnt)) {
     const int qp = 128 * (i - 1) + 4 * lane;
     const bool in_kp = (qp >> 5) < ksteps;
-    prep_epilogue(tmem + prep_region(n_cols, w >> 2, prep_dbuf(n_cols) ? (i - 1) & 1 : 0), N,
+    prep_epilogue(tmem + prep_region<kBias>(n_cols, w >> 2, kBias ? 0 : (i - 1) & 1), N,
                   d.img + img_off(rg, col, in_kp ? qp : 0), d.plane_bytes, in_kp);
   }
 #pragma unroll
@@ -594,14 +618,19 @@ __device__ __forceinline__ int find_owner(const P* __restrict__ prefix, int num,
   return lo;
 }
 
+// Compiled twice: kBias = false for descriptors with N <= 15, true for N > 15 (the host
+// launches each on its own range of the descriptor array; prefix values are absolute and the
+// grid's blocks start at block block0 of that numbering).
+template <bool kBias>
 __global__ void __launch_bounds__(kPrepThreads, 2)
     prep_kernel(const ggemm_prep_desc_t* __restrict__ descs, const int* __restrict__ prefix,
-                int num, DevCounters* cnt) {
+                int num, int block0, DevCounters* cnt) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  const int owner = find_owner(prefix, num, (int)blockIdx.x);
+  const int bl = block0 + (int)blockIdx.x;
+  const int owner = find_owner(prefix, num, bl);
   const ggemm_prep_desc_t d = descs[owner];
-  if (d.N < 1 || d.N > kMaxModuli || d.rows <= 0) return;
+  if (d.N < 1 || d.N > kMaxModuli || d.rows <= 0 || prep_needs_bias(d.N) != kBias) return;
   const int n_cols = (4 * (d.N + 1) + 15) / 16 * 16;
   build_weights(sm, d.N, n_cols);
   if (threadIdx.x == 0) {
@@ -622,9 +651,14 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem;
-  const int blk = (int)blockIdx.x - prefix[owner];
-  if (d.kind == 0) prep_rows_block(d, blk, cnt, sm, tmem, n_cols);
-  else prep_cols_block(d, blk, cnt, sm, tmem, n_cols);
+  if (kBias) {  // the half's accumulator starts from the bias (ordered before the
+                           // first MMA by the round's fence / barrier)
+    prep_bias_acc(tmem + prep_region<kBias>(n_cols, threadIdx.x >> 7, 0), n_cols);
+    tmem_st_wait();
+  }
+  const int blk = bl - prefix[owner];
+  if (d.kind == 0) prep_rows_block<kBias>(d, blk, cnt, sm, tmem, n_cols);
+  else prep_cols_block<kBias>(d, blk, cnt, sm, tmem, n_cols);
   // a half that gave up may still have MMAs in flight (at most its last two rounds, since
   // every round waits for the one before): let them finish (bounded) first
   __syncthreads();
@@ -1389,7 +1423,9 @@ int upload_tables_current_device() {
   if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kGemmSmem) != cudaSuccess)
     return 3;
-  if (cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(prep_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kPrepSmem) != cudaSuccess ||
+      cudaFuncSetAttribute(prep_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kPrepSmem) != cudaSuccess)
     return 3;
   g_gemm_attr[dev] = true;
@@ -1406,10 +1442,21 @@ int current_device_sms() {
   return g_sms[dev] > 0 ? g_sms[dev] : 148;
 }
 
-int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, int num, int total_blocks,
-                DevCounters* cnt, cudaStream_t s) {
-  if (num <= 0 || total_blocks <= 0) return 0;
-  prep_kernel<<<total_blocks, kPrepThreads, kPrepSmem, s>>>(d_descs, d_prefix, num, cnt);
+int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, int num, int num_lo,
+                int blocks_lo, int total_blocks, DevCounters* cnt, cudaStream_t s,
+                int* launches) {
+  int n = 0;
+  if (num_lo > 0 && blocks_lo > 0) {
+    prep_kernel<false><<<blocks_lo, kPrepThreads, kPrepSmem, s>>>(d_descs, d_prefix, num_lo, 0,
+                                                                   cnt);
+    ++n;
+  }
+  if (num > num_lo && total_blocks > blocks_lo) {
+    prep_kernel<true><<<total_blocks - blocks_lo, kPrepThreads, kPrepSmem, s>>>(
+        d_descs + num_lo, d_prefix + num_lo, num - num_lo, blocks_lo, cnt);
+    ++n;
+  }
+  if (launches) *launches += n;
   return (int)cudaGetLastError();
 }
 

@@ -94,8 +94,13 @@ int current_device_sms();
 
 // Launchers: one kernel each on `s`.  prefix: device array of num+1 exclusive block / tile
 // prefix sums.  Return cudaError_t of the launch.
-int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, int num, int total_blocks,
-                DevCounters* cnt, cudaStream_t s);
+// Prep: descriptors [0, num_lo) have N <= 15 (prep_needs_bias false) and own blocks
+// [0, blocks_lo) of the prefix numbering; the rest have N > 15.  One launch per non-empty range
+// (the kernel is compiled once per case); *launches, when given, is increased by their number.
+__host__ __device__ constexpr inline bool prep_needs_bias(int N) { return N > 15; }
+int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, int num, int num_lo,
+                int blocks_lo, int total_blocks, DevCounters* cnt, cudaStream_t s,
+                int* launches = nullptr);
 int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long long total_tiles,
                 DevCounters* cnt, cudaStream_t s);
 // Blocks per job: recon_job_blocks.

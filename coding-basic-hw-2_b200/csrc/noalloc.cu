@@ -205,6 +205,7 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
   if (nprep &&
       launch_prep(reinterpret_cast<const ggemm_prep_desc_t*>(db + offsetof(NoAllocDescs, prep)),
                   reinterpret_cast<const int*>(db + offsetof(NoAllocDescs, prep_prefix)), nprep,
+                  prep_needs_bias(N) ? 0 : nprep, prep_needs_bias(N) ? 0 : prep_blocks_total,
                   prep_blocks_total, cnt, stream))
     return GGEMM_ERR_NUMERICS;
   if (d.job_prefix[1] > 0 &&
