@@ -126,6 +126,8 @@ class ReconDesc(ctypes.Structure):
 # Product layouts between the residue GEMM and the reconstruct (ggemm_stages.h).
 PRODUCTS_INT32 = 0
 PRODUCTS_DIGITS = 1
+PRODUCTS_DIGITS_QSCALED = 2  # GEMM stage only: A images prepared with PREP_QSCALED
+PREP_QSCALED = 2  # flag in PrepDesc.kind: plane l holds residues of q_l x
 
 
 def digit_plane_bytes(m, n):

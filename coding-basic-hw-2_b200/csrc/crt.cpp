@@ -163,6 +163,12 @@ void make_dev_tables(const CrtTables& t, DevTables* d) {
     d->T[N] = t.T[N];
     for (int l = 0; l < kMaxModuli; ++l) {
       d->qinv[N][l] = (uint32_t)t.qinv[N][l];
+      const uint32_t p = (uint32_t)t.p[l];
+      for (int i = 0; i < kByteDigits; ++i) {
+        const uint32_t w = (uint32_t)(d->wb[l][i] < 0 ? d->wb[l][i] + (int)p : d->wb[l][i]);
+        const uint32_t s = (uint32_t)((uint64_t)w * (uint32_t)t.qinv[N][l] % p);
+        d->wbq[N][l][i] = (int8_t)(2 * s > p ? (int)s - (int)p : (int)s);
+      }
       d->s1[N][l] = t.s1[N][l];
       d->s2[N][l] = t.s2[N][l];
     }

@@ -38,6 +38,7 @@ struct DevTables {
   float pf[kMaxModuli];
   float invpf[kMaxModuli];
   int8_t wb[kMaxModuli][kByteDigits];  // 2^(8 i) mod p_l, symmetric representative
+  int8_t wbq[kMaxModuli + 1][kMaxModuli][kByteDigits];  // q_l 2^(8 i) mod p_l (N moduli)
   double T[kMaxModuli + 1];
   // reconstruct
   uint32_t p[kMaxModuli];

@@ -291,6 +291,15 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
   int* order = h->order.data();
   for (Chunk& ch : h->chunks) {
     const int cid = (int)(&ch - h->chunks.data());
+    // The A images of a chunk are q-scaled (GGEMM_PREP_QSCALED) when every problem of the chunk
+    // takes the digit layout and has its A image's moduli count: the GEMM epilogue then
+    // skips the modular product by q_l.
+    ch.qscale = true;
+    for (int j = ch.first; j < ch.first + ch.count; ++j) {
+      const ggemm_problem_t& p = probs[emu[j]];
+      const int N = plan[emu[j]].num_moduli;
+      if (!use_y8(p.m, p.n, N) || h->ua_n[h->ua_of[j]] != N) ch.qscale = false;
+    }
     // prep descriptors: unique A / B operands first placed in this chunk
     int np = 0;
     for (int j = ch.first; j < ch.first + ch.count; ++j) {
@@ -315,7 +324,7 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         d.rows = p.m;
         d.k = p.k;
         d.N = h->ua_n[ua];
-        d.kind = 0;
+        d.kind = ch.qscale ? GGEMM_PREP_QSCALED : 0;
         d.img = h->imgA + h->ua_img[ua];
         d.plane_bytes = (long long)align_up(ggemm_img_plane_bytes(p.m, p.k), kAlign);
         d.ws = h->wsA + h->ua_ws[ua];
@@ -396,7 +405,7 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       base.c_plane = (long long)c_plane_elems(p.m, p.n);
       base.y_plane = (long long)y8_plane_bytes(p.m, p.n);
       base.N = N;
-      base.y8 = use_y8(p.m, p.n, N) ? 1 : 0;
+      base.y8 = use_y8(p.m, p.n, N) ? (ch.qscale ? 2 : 1) : 0;
       base.m = p.m;
       base.n = p.n;
       base.ksteps = (p.k + 31) / 32;

@@ -188,8 +188,10 @@ __device__ __forceinline__ void put_slot(PrepSmem& sm, int half, int bf, int rho
 }
 
 // Block-diagonal weights: row n = 4 l + e of the B operand holds plane l's weights in K step
-// (slot) e and zeros elsewhere; planes l > N are zero.
-__device__ void build_weights(PrepSmem& sm, int N, int n_cols) {
+// (slot) e and zeros elsewhere; planes l > N are zero.  qscale (GGEMM_PREP_QSCALED): the weights
+// of plane l < N are q_l 2^(8 i) mod p_l (symmetric), so that the plane holds the residue of
+// q_l x instead of x (q_l the CRT factor the reconstruct applies to plane l's digits).
+__device__ void build_weights(PrepSmem& sm, int N, int n_cols, bool qscale) {
   const int rg = n_cols / 8;
   for (int c = threadIdx.x; c < 8 * n_cols; c += blockDim.x) {
     const int half = c & 1, n = (c >> 1) % n_cols, e = (c >> 1) / n_cols;
@@ -200,9 +202,10 @@ __device__ void build_weights(PrepSmem& sm, int N, int n_cols) {
       for (int b = 0; b < 16; ++b) {
         const int dd = 16 * half + b;
         int v = 0;
+        const int8_t* wl = qscale ? c_tab.wbq[N][l] : c_tab.wb[l];
         if (l == N) v = dd == 23 ? 1 : 0;
-        else if (dd < 12) v = c_tab.wb[l][dd];
-        else if (dd < 23) v = c_tab.wb[l][dd - 11];
+        else if (dd < 12) v = wl[dd];
+        else if (dd < 23) v = wl[dd - 11];
         w[b >> 2] |= (uint32_t)(v & 255) << (8 * (b & 3));
       }
     }
@@ -632,7 +635,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
   const ggemm_prep_desc_t d = descs[owner];
   if (d.N < 1 || d.N > kMaxModuli || d.rows <= 0 || prep_needs_bias(d.N) != kBias) return;
   const int n_cols = (4 * (d.N + 1) + 15) / 16 * 16;
-  build_weights(sm, d.N, n_cols);
+  build_weights(sm, d.N, n_cols, (d.kind & GGEMM_PREP_QSCALED) != 0);
   if (threadIdx.x == 0) {
     for (int h = 0; h < 2; ++h) {
       mbar_init(&sm.bar[h][0], 1);
@@ -657,7 +660,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     tmem_st_wait();
   }
   const int blk = bl - prefix[owner];
-  if (d.kind == 0) prep_rows_block<kBias>(d, blk, cnt, sm, tmem, n_cols);
+  if ((d.kind & 1) == 0) prep_rows_block<kBias>(d, blk, cnt, sm, tmem, n_cols);
   else prep_cols_block<kBias>(d, blk, cnt, sm, tmem, n_cols);
   // a half that gave up may still have MMAs in flight (at most its last two rounds, since
   // every round waits for the one before): let them finish (bounded) first
@@ -742,13 +745,16 @@ struct DigitCtx {
   bool digit;  // false: the abs plane (int32 output)
 };
 
-__device__ __forceinline__ DigitCtx digit_ctx(int plane, int N) {
+// qscaled: the A images hold residues of q_l a (GGEMM_PREP_QSCALED), corr is then the multiple
+// of p_l that crt_digit_q adds.
+__device__ __forceinline__ DigitCtx digit_ctx(int plane, int N, bool qscaled) {
   DigitCtx dc{1u, 0u, 0u, 0u, plane < N};
   if (dc.digit) {
     dc.p = c_tab.p[plane];
     dc.magic = c_tab.magic[plane];
     dc.q = c_tab.qinv[N][plane];
-    dc.corr = (dc.p - 0x80000000u % dc.p) % dc.p * dc.q % dc.p;
+    dc.corr = qscaled ? (0x80000000u + dc.p - 1u) / dc.p * dc.p
+                      : (dc.p - 0x80000000u % dc.p) % dc.p * dc.q % dc.p;
   }
   return dc;
 }
@@ -761,15 +767,31 @@ __device__ __forceinline__ uint32_t crt_digit(uint32_t c, const DigitCtx& dc) {
   return min(y, y - dc.p);
 }
 
+// Digit of a product of q-scaled residues: c = C'_l = q_l C_l (mod p_l), so y_l = c mod p_l.
+// u = c + corr (corr = p ceil(2^31 / p)) lies in [0, 2^32) because |c| <= kMaxKExact 127^2
+// for odd p (for p = 256 only u's low byte matters and a wrap is harmless); the quotient
+// estimate umulhi(u, floor(2^32 / p)) is low by at most one, so r < 2p.
+__device__ __forceinline__ uint32_t crt_digit_q(uint32_t c, const DigitCtx& dc) {
+  const uint32_t u = c + dc.corr;
+  const uint32_t r = u - __umulhi(u, dc.magic) * dc.p;
+  return min(r, r - dc.p);
+}
+
+template <bool kQ>
+__device__ __forceinline__ uint32_t digit_of(uint32_t c, const DigitCtx& dc) {
+  return kQ ? crt_digit_q(c, dc) : crt_digit(c, dc);
+}
+
 // One 32-column record of one row: 32 digit bytes (two 16-byte stores) or 32 int32 (eight).
+template <bool kQ>
 __device__ __forceinline__ void emit_record(const uint32_t (&v)[32], const DigitCtx& dc,
                                             uint8_t* ydst, int32_t* ldst) {
   if (dc.digit) {
     uint32_t w[8];
 #pragma unroll
     for (int g = 0; g < 8; ++g)
-      w[g] = crt_digit(v[4 * g], dc) | (crt_digit(v[4 * g + 1], dc) << 8) |
-             (crt_digit(v[4 * g + 2], dc) << 16) | (crt_digit(v[4 * g + 3], dc) << 24);
+      w[g] = digit_of<kQ>(v[4 * g], dc) | (digit_of<kQ>(v[4 * g + 1], dc) << 8) |
+             (digit_of<kQ>(v[4 * g + 2], dc) << 16) | (digit_of<kQ>(v[4 * g + 3], dc) << 24);
     uint4* d = reinterpret_cast<uint4*>(ydst);
     d[0] = make_uint4(w[0], w[1], w[2], w[3]);
     d[1] = make_uint4(w[4], w[5], w[6], w[7]);
@@ -778,6 +800,35 @@ __device__ __forceinline__ void emit_record(const uint32_t (&v)[32], const Digit
 #pragma unroll
     for (int g = 0; g < 8; ++g)
       d[g] = make_int4((int)v[4 * g], (int)v[4 * g + 1], (int)v[4 * g + 2], (int)v[4 * g + 3]);
+  }
+}
+
+// Digit-layout epilogue of one tile for one thread (TMEM lane = row of the tile): nch records
+// of 32 columns.  kQ: the job's A images are q-scaled (GemmJob::y8 == 2).
+template <bool kQ>
+__device__ __forceinline__ void gemm_digit_records(const GemmJob& jb, const TileInfo& ti, int row,
+                                                   uint32_t taddr, int nch) {
+  const int pl = jb.plane0 + ti.plane;
+  const DigitCtx dc = digit_ctx(pl, jb.N, kQ);
+  const long long rec0 = ((long long)ti.tn * (jb.bn / 32) * jb.m + row) * 32;
+  uint8_t* ydst = jb.Y + (long long)pl * jb.y_plane + rec0;
+  int32_t* ldst = reinterpret_cast<int32_t*>(jb.Y + (long long)jb.N * jb.y_plane) + rec0;
+  const long long cstep = (long long)jb.m * 32;  // one record column
+  const bool live = row < jb.m;
+  // two register buffers: the TMEM load of chunk c + 1 overlaps the digits of chunk c
+  uint32_t va[32], vb[32];
+  tmem_ld_32x32b_x32(taddr, va);
+  tmem_ld_wait(va);
+#pragma unroll 1
+  for (int c = 0; c < nch; c += 2) {
+    if (c + 1 < nch) tmem_ld_32x32b_x32(taddr + (uint32_t)((c + 1) * 32), vb);
+    if (live) emit_record<kQ>(va, dc, ydst + c * cstep, ldst + c * cstep);
+    if (c + 1 < nch) {
+      tmem_ld_wait(vb);
+      if (c + 2 < nch) tmem_ld_32x32b_x32(taddr + (uint32_t)((c + 2) * 32), va);
+      if (live) emit_record<kQ>(vb, dc, ydst + (c + 1) * cstep, ldst + (c + 1) * cstep);
+      if (c + 2 < nch) tmem_ld_wait(va);
+    }
   }
 }
 
@@ -928,29 +979,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t taddr = tmem + (uint32_t)(buf * kGemmBNMax) + ((uint32_t)(quad * 32) << 16);
       // record columns of this tile that lie inside the problem
       const int nch = min(jb.bn, jb.n - ti.tn * jb.bn + 31) / 32;
-      if (jb.y8) {
-        const int pl = jb.plane0 + ti.plane;
-        const DigitCtx dc = digit_ctx(pl, jb.N);
-        const long long rec0 = ((long long)ti.tn * (jb.bn / 32) * jb.m + row) * 32;
-        uint8_t* ydst = jb.Y + (long long)pl * jb.y_plane + rec0;
-        int32_t* ldst = reinterpret_cast<int32_t*>(jb.Y + (long long)jb.N * jb.y_plane) + rec0;
-        const long long cstep = (long long)jb.m * 32;  // one record column
-        const bool live = row < jb.m;
-        // two register buffers: the TMEM load of chunk c + 1 overlaps the digits of chunk c
-        uint32_t va[32], vb[32];
-        tmem_ld_32x32b_x32(taddr, va);
-        tmem_ld_wait(va);
-#pragma unroll 1
-        for (int c = 0; c < nch; c += 2) {
-          if (c + 1 < nch) tmem_ld_32x32b_x32(taddr + (uint32_t)((c + 1) * 32), vb);
-          if (live) emit_record(va, dc, ydst + c * cstep, ldst + c * cstep);
-          if (c + 1 < nch) {
-            tmem_ld_wait(vb);
-            if (c + 2 < nch) tmem_ld_32x32b_x32(taddr + (uint32_t)((c + 2) * 32), va);
-            if (live) emit_record(vb, dc, ydst + (c + 1) * cstep, ldst + (c + 1) * cstep);
-            if (c + 2 < nch) tmem_ld_wait(va);
-          }
-        }
+      if (jb.y8 == 2) {
+        gemm_digit_records<true>(jb, ti, row, taddr, nch);
+      } else if (jb.y8) {
+        gemm_digit_records<false>(jb, ti, row, taddr, nch);
       } else {
         int32_t* C = jb.C + (long long)ti.plane * jb.c_plane;
 #pragma unroll 1

@@ -68,7 +68,7 @@ constexpr int kPrepThreads = 256, kReconThreads = 256, kReconPerThread = 4;
 // Blocks of one prep descriptor (A: 32 rows per block, B: 8 columns per block).
 inline int prep_blocks(const ggemm_prep_desc_t& d) {
   if (d.rows <= 0 || d.k < 0) return 0;
-  return d.kind == 0 ? (d.rows + 31) / 32 : (d.rows + 7) / 8;
+  return (d.kind & 1) == 0 ? (d.rows + 31) / 32 : (d.rows + 7) / 8;
 }
 inline long long recon_blocks(const ggemm_recon_desc_t& d) {
   const long long mn = (long long)d.m * (long long)d.n;

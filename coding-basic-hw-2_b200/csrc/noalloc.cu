@@ -139,7 +139,7 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
     a.rows = q.m;
     a.k = q.k;
     a.N = N;
-    a.kind = 0;
+    a.kind = digits ? GGEMM_PREP_QSCALED : 0;  // q-scaled residues for the digit epilogue
     a.img = reinterpret_cast<int8_t*>(base + off_ia);
     a.plane_bytes = (long long)pa;
     a.ws = reinterpret_cast<int32_t*>(base + off_wa);
@@ -169,7 +169,7 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
   j.c_plane = (long long)cp;
   j.y_plane = (long long)y8_plane_bytes(q.m, q.n);
   j.N = N;
-  j.y8 = digits ? 1 : 0;
+  j.y8 = digits ? 2 : 0;
   j.m = q.m;
   j.n = q.n;
   j.ksteps = (q.k + 31) / 32;

@@ -50,7 +50,7 @@ extern "C" int ggemm_stage_prep(const ggemm_prep_desc_t* descs, int num, void* s
   std::memcpy(sd, descs, (size_t)num * sizeof(ggemm_prep_desc_t));
   for (int i = 0; i < num; ++i) {
     const ggemm_prep_desc_t& d = descs[i];
-    if (d.rows < 0 || d.k < 0 || d.N < 1 || d.N > kMaxModuli || (d.kind != 0 && d.kind != 1))
+    if (d.rows < 0 || d.k < 0 || d.N < 1 || d.N > kMaxModuli || (d.kind & ~(1 | GGEMM_PREP_QSCALED)))
       return GGEMM_ERR_INVALID;
     if (d.rows > 0 && (!d.X || !d.img || !d.ws)) return GGEMM_ERR_INVALID;
     if (((uintptr_t)d.img & 15) || (d.plane_bytes & 15) ||
@@ -94,7 +94,8 @@ extern "C" int ggemm_stage_gemm(const ggemm_gemm_desc_t* descs, int num, void* s
     const ggemm_gemm_desc_t& d = descs[i];
     if (d.m < 0 || d.n < 0 || d.k < 0 || d.planes < 0 || d.k > kMaxKExact)
       return GGEMM_ERR_INVALID;
-    const bool digits = d.layout == GGEMM_PRODUCTS_DIGITS;
+    const bool qscaled = d.layout == GGEMM_PRODUCTS_DIGITS_QSCALED;
+    const bool digits = d.layout == GGEMM_PRODUCTS_DIGITS || qscaled;
     if (!digits && d.layout != GGEMM_PRODUCTS_INT32) return GGEMM_ERR_INVALID;
     GemmJob j{};
     j.A = d.A;
@@ -110,7 +111,7 @@ extern "C" int ggemm_stage_gemm(const ggemm_gemm_desc_t* descs, int num, void* s
     j.ksteps = (d.k + 31) / 32;
     j.planes = (d.m > 0 && d.n > 0 && d.k > 0) ? d.planes : 0;
     j.N = d.N;
-    j.y8 = digits ? 1 : 0;
+    j.y8 = qscaled ? 2 : digits ? 1 : 0;
     set_gemm_tiling(j);
     if (j.planes > 0) {
       if (!d.A || !d.B || !d.C || ((uintptr_t)d.A & 15) || ((uintptr_t)d.B & 15) ||

@@ -50,6 +50,9 @@ static inline size_t ggemm_img_offset(int rows, int r, int q) {
 
 /* One operand of one problem for prep.  kind 0: the rows of a column-major A (element (r, q)
  * at X[r + q*ld]); kind 1: the columns of a column-major B (element (r, q) at X[q + r*ld]).
+ * kind | GGEMM_PREP_QSCALED (extension): residue plane l holds the symmetric residue of
+ * q_l x instead of x, q_l = ((P_N / p_l)^-1 mod p_l) the CRT factor of plane l, so that the
+ * residue GEMM's digit epilogue skips one modular product (GGEMM_PRODUCTS_DIGITS_QSCALED).
  * img: N+1 planes (N residue planes, then the abs plane) at stride plane_bytes.
  * ws: 4*rows int32 {shift | abs shift | ||dX_r|| (float bits) | ||X'_r|| (float bits)}. */
 typedef struct {
@@ -74,6 +77,11 @@ typedef struct {
  *   N + 4 bytes per entry instead of 4 (N + 1). */
 #define GGEMM_PRODUCTS_INT32 0
 #define GGEMM_PRODUCTS_DIGITS 1
+/* Residue GEMM layout only (extension): the digit layout, computed from products of which one
+ * operand's images were prepared with GGEMM_PREP_QSCALED (the digits are C'_l mod p_l; the
+ * output is byte-identical to GGEMM_PRODUCTS_DIGITS from unscaled images). */
+#define GGEMM_PRODUCTS_DIGITS_QSCALED 2
+#define GGEMM_PREP_QSCALED 2
 
 /* Bytes of one digit plane of an m x n problem (256-byte multiple). */
 static inline size_t ggemm_digit_plane_bytes(int m, int n) {

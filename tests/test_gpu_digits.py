@@ -67,7 +67,8 @@ def _rand_planes(rng, P, rows, k, lo=-128, hi=128):
     return a
 
 
-def run_gemm_digits(g2, A8s, B8s, ks, Ns):
+def run_gemm_digits(g2, A8s, B8s, ks, Ns, layout=None):
+    layout = g2.PRODUCTS_DIGITS if layout is None else layout
     descs = (g2.GemmDesc * len(A8s))()
     keep, outs = [], []
     for i, (A8, B8, k, N) in enumerate(zip(A8s, B8s, ks, Ns)):
@@ -87,7 +88,7 @@ def run_gemm_digits(g2, A8s, B8s, ks, Ns):
         keep += [da, db]
         outs.append((dy, m, n, N, yp))
         descs[i] = g2.GemmDesc(da.data_ptr(), db.data_ptr(), dy.data_ptr(), pa, pb, yp, m, n, k,
-                               P, N, g2.PRODUCTS_DIGITS)
+                               P, N, layout)
     scr, cnt = _scratch(g2, len(A8s)), _counters()
     assert g2.lib.ggemm_stage_gemm(descs, len(A8s), scr.data_ptr(), scr.numel(), cnt.data_ptr(),
                                    _stream()) == 0
@@ -123,6 +124,49 @@ def test_gemm_digits_grouped(g2, cuda, tables):
         C = _exact(A8, B8)
         assert np.array_equal(Y.astype(np.int64), digits_of(C, N, tables)), (m, n, k, N)
         assert np.array_equal(L.astype(np.int64), C[N]), (m, n, k, N)
+
+
+def qscale(A8: np.ndarray, N: int, t) -> np.ndarray:
+    """A residue planes -> q_l-scaled planes (GGEMM_PREP_QSCALED); the abs plane is kept."""
+    out = A8.copy()
+    for l in range(N):
+        p, q = int(t["p"][l]), int(t["qinv"][N][l])
+        s = (A8[l].astype(np.int64) % p) * q % p
+        out[l] = (np.where(2 * s > p, s - p, s) & 255).astype(np.uint8).view(np.int8)
+    return out
+
+
+def test_gemm_digits_qscaled(g2, cuda, tables):
+    """GGEMM_PRODUCTS_DIGITS_QSCALED: from q-scaled A images the epilogue reduces C'_l mod p_l
+    only; the digits equal those of the unscaled products."""
+    rng = np.random.default_rng(199)
+    A8s, As, B8s, ks, Ns = [], [], [], [], []
+    for m, n, k, N in DIGIT_SHAPES:
+        A8 = _rand_planes(rng, N + 1, m, k)
+        A8s.append(A8)
+        As.append(qscale(A8, N, tables))
+        B8s.append(_rand_planes(rng, N + 1, n, k))
+        ks.append(k)
+        Ns.append(N)
+    outs = run_gemm_digits(g2, As, B8s, ks, Ns, g2.PRODUCTS_DIGITS_QSCALED)
+    for (m, n, k, N), A8, B8, (Y, L) in zip(DIGIT_SHAPES, A8s, B8s, outs):
+        C = _exact(A8, B8)
+        assert np.array_equal(Y.astype(np.int64), digits_of(C, N, tables)), (m, n, k, N)
+        assert np.array_equal(L.astype(np.int64), C[N]), (m, n, k, N)
+
+
+@pytest.mark.parametrize("sa,sb", [(-128, -128), (-128, 127), (127, -128), (127, 127)])
+def test_gemm_digits_qscaled_int32_extremes(g2, cuda, tables, sa, sb):
+    """The q-scaled digit at the int32 limit: k = 131040 with constant scaled residues, so that
+    C'_l sits at +-128^2 k or +-127^2 k."""
+    k, N = 131040, 20
+    A8 = np.full((N + 1, 8, k), sa, dtype=np.int8)
+    B8 = np.full((N + 1, 40, k), sb, dtype=np.int8)
+    Y, L = run_gemm_digits(g2, [A8], [B8], [k], [N], g2.PRODUCTS_DIGITS_QSCALED)[0]
+    # A8 here already stands for the scaled residues: the digit is C' mod p_l
+    p = tables["p"][:N].astype(np.int64)[:, None, None]
+    assert np.array_equal(Y.astype(np.int64), np.full((N, 8, 40), sa * sb * k, np.int64) % p)
+    assert np.array_equal(L.astype(np.int64), np.full((8, 40), sa * sb * k, np.int64))
 
 
 @pytest.mark.parametrize("sa,sb", [(-128, -128), (-128, 127), (127, -128)])

@@ -10,7 +10,7 @@ import ctypes
 import numpy as np
 import pytest
 
-from g2util import col_major, gen
+from g2util import col_major, decode_tables, gen
 
 torch = pytest.importorskip("torch")
 
@@ -109,6 +109,42 @@ def test_prep_matches_oracle(g2, oracle, cuda, rows, k, N, kind, phi, special):
             rr, qq = r & 7, q & 31
             off = ((q >> 5) * rg + (r >> 3)) * 256 + rr * 32 + (((qq >> 4) ^ (rr >> 2)) << 4) + (qq & 15)
             assert np.all(img_h[l * pb + off] == 0)
+
+
+def qscale_planes(planes: np.ndarray, N: int, t) -> np.ndarray:
+    """Residue planes of x -> residue planes of q_l x (GGEMM_PREP_QSCALED): the symmetric
+    representative for odd p_l, the two's complement low byte for p_0 = 256; abs plane kept."""
+    out = planes.copy()
+    for l in range(N):
+        p, q = int(t["p"][l]), int(t["qinv"][N][l])
+        s = (planes[l].astype(np.int64) % p) * q % p
+        s = np.where(2 * s > p, s - p, s)
+        out[l] = (s & 255).astype(np.uint8).view(np.int8)
+    return out
+
+
+@pytest.mark.parametrize("rows,k,N,kind,phi,special",
+                         [c for c in PREP_CASES if c[3] == 0 and c[5] in (None, "nan", "tiny")])
+def test_prep_qscaled_matches_oracle(g2, oracle, cuda, rows, k, N, kind, phi, special):
+    """kind | GGEMM_PREP_QSCALED: plane l < N holds the residues of q_l x, the workspace and the
+    abs plane are those of the unscaled prep."""
+    rng = np.random.default_rng(2000 + rows * 7 + k + N * 13)
+    mat = gen(rng, (rows, k), phi)
+    if special == "tiny":
+        mat *= 2.0 ** -700
+    elif special == "nan":
+        mat[2, 17] = np.nan
+    ld = rows + 3
+    X = col_major(mat, ld)
+    planes, ws, (cnt, status), _, _ = run_prep(g2, X, rows, k, ld, N, kind | g2.PREP_QSCALED)
+    ref_planes, ref_ws, ref_nf = oracle.prep(X, rows, k, ld, N, kind)
+    assert status == 0
+    np.testing.assert_array_equal(ws, ref_ws)
+    want = qscale_planes(ref_planes, N, decode_tables(oracle.tables_bytes()))
+    for l in range(N + 1):
+        bad = np.argwhere(planes[l] != want[l])
+        assert bad.size == 0, f"plane {l}: {len(bad)} mismatches, first {bad[:4].tolist()}"
+    assert cnt[0] == ref_nf
 
 
 def run_gemm(g2, A8s, B8s, ks):
