@@ -16,6 +16,7 @@
 #include <cmath>
 #include <cstdio>
 #include <mutex>
+#include <vector>
 
 #include "crt.hpp"
 #include "kernels.cuh"
@@ -187,32 +188,18 @@ __device__ __forceinline__ void put_slot(PrepSmem& sm, int half, int bf, int rho
   *reinterpret_cast<uint4*>(base + (16 ^ sw)) = hi;
 }
 
-// Block-diagonal weights: row n = 4 l + e of the B operand holds plane l's weights in K step
-// (slot) e and zeros elsewhere; planes l > N are zero.  qscale (GGEMM_PREP_QSCALED): the weights
-// of plane l < N are q_l 2^(8 i) mod p_l (symmetric), so that the plane holds the residue of
-// q_l x instead of x (q_l the CRT factor the reconstruct applies to plane l's digits).
-__device__ void build_weights(PrepSmem& sm, int N, int n_cols, bool qscale) {
-  const int rg = n_cols / 8;
-  for (int c = threadIdx.x; c < 8 * n_cols; c += blockDim.x) {
-    const int half = c & 1, n = (c >> 1) % n_cols, e = (c >> 1) / n_cols;
-    const int l = n >> 2;
-    uint32_t w[4] = {0u, 0u, 0u, 0u};
-    if ((n & 3) == e && l <= N) {
-#pragma unroll
-      for (int b = 0; b < 16; ++b) {
-        const int dd = 16 * half + b;
-        int v = 0;
-        const int8_t* wl = qscale ? c_tab.wbq[N][l] : c_tab.wb[l];
-        if (l == N) v = dd == 23 ? 1 : 0;
-        else if (dd < 12) v = wl[dd];
-        else if (dd < 23) v = wl[dd - 11];
-        w[b >> 2] |= (uint32_t)(v & 255) << (8 * (b & 3));
-      }
-    }
-    const int rr = n & 7;
-    uint8_t* dst = sm.wts + (e * rg + (n >> 3)) * 256 + rr * 32 + ((half ^ (rr >> 2)) << 4);
-    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-  }
+// Block-diagonal weights (the MMA's B operand, K-major, 32-byte swizzle), one image per
+// (qscale, N) built on the host (make_prep_weight_images) and copied to shared memory by every
+// block: row n = 4 l + e holds plane l's weights in K step (slot) e and zeros elsewhere; planes
+// l > N are zero.  qscale (GGEMM_PREP_QSCALED): the weights of plane l < N are q_l 2^(8 i) mod p_l
+// (symmetric), so that the plane holds the residue of q_l x instead of x (q_l the CRT factor the
+// reconstruct applies to plane l's digits).
+__device__ uint8_t g_prep_wts[2][kMaxModuli + 1][kPrepWBytes];
+
+__device__ __forceinline__ void load_weights(PrepSmem& sm, int N, int n_cols, bool qscale) {
+  const uint4* src = reinterpret_cast<const uint4*>(g_prep_wts[qscale ? 1 : 0][N]);
+  uint4* dst = reinterpret_cast<uint4*>(sm.wts);
+  for (int c = threadIdx.x; c < 8 * n_cols; c += blockDim.x) dst[c] = src[c];
 }
 
 // With single-buffered accumulators (N > 15) they start from kPrepBias = bits(1.5 * 2^23)
@@ -621,6 +608,17 @@ __device__ __forceinline__ int find_owner(const P* __restrict__ prefix, int num,
   return lo;
 }
 
+// find_owner by one warp (every warp of a block computes the same value): lane L counts the
+// entries i = L (mod 32) with prefix[i] <= x, eight loads in flight at a time (one memory round
+// trip per 256 entries instead of one per bisection step).  Call by all 32 lanes.
+template <typename P>
+__device__ __forceinline__ int find_owner_warp(const P* __restrict__ prefix, int num, P x) {
+  int c = 0;
+#pragma unroll 8
+  for (int i = threadIdx.x & 31; i < num; i += 32) c += prefix[i] <= x ? 1 : 0;
+  return __reduce_add_sync(0xFFFFFFFFu, c) - 1;
+}
+
 // Compiled twice: kBias = false for descriptors with N <= 15, true for N > 15 (the host
 // launches each on its own range of the descriptor array; prefix values are absolute and the
 // grid's blocks start at block block0 of that numbering).
@@ -631,11 +629,11 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int bl = block0 + (int)blockIdx.x;
-  const int owner = find_owner(prefix, num, bl);
+  const int owner = find_owner_warp(prefix, num, bl);
   const ggemm_prep_desc_t d = descs[owner];
   if (d.N < 1 || d.N > kMaxModuli || d.rows <= 0 || prep_needs_bias(d.N) != kBias) return;
   const int n_cols = (4 * (d.N + 1) + 15) / 16 * 16;
-  build_weights(sm, d.N, n_cols, (d.kind & GGEMM_PREP_QSCALED) != 0);
+  load_weights(sm, d.N, n_cols, (d.kind & GGEMM_PREP_QSCALED) != 0);
   if (threadIdx.x == 0) {
     for (int h = 0; h < 2; ++h) {
       mbar_init(&sm.bar[h][0], 1);
@@ -1421,7 +1419,7 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
 __global__ void __launch_bounds__(kReconThreads, 2)
     recon_kernel(const ggemm_recon_desc_t* __restrict__ descs,
                  const long long* __restrict__ prefix, int num, int mode, DevCounters* cnt) {
-  const int owner = find_owner(prefix, num, (long long)blockIdx.x);
+  const int owner = find_owner_warp(prefix, num, (long long)blockIdx.x);
   const ggemm_recon_desc_t d = descs[owner];
   const long long local = (long long)blockIdx.x - prefix[owner];
   unsigned n_unc = 0, n_rep = 0, n_saf = 0;
@@ -1438,6 +1436,32 @@ int g_sms[64] = {0};
 bool g_gemm_attr[64] = {false};
 }  // namespace
 
+// Host copy of the prep weight images g_prep_wts[qscale][N] (layout above).
+static std::vector<uint8_t> make_prep_weight_images(const DevTables& dt) {
+  std::vector<uint8_t> out(sizeof(g_prep_wts), 0);
+  for (int qs = 0; qs < 2; ++qs)
+    for (int N = 1; N <= kMaxModuli; ++N) {
+      uint8_t* img = out.data() + ((size_t)qs * (kMaxModuli + 1) + N) * kPrepWBytes;
+      const int n_cols = (4 * (N + 1) + 15) / 16 * 16, rg = n_cols / 8;
+      for (int c = 0; c < 8 * n_cols; ++c) {
+        const int half = c & 1, n = (c >> 1) % n_cols, e = (c >> 1) / n_cols;
+        const int l = n >> 2, rr = n & 7;
+        uint8_t* dst = img + (e * rg + (n >> 3)) * 256 + rr * 32 + ((half ^ (rr >> 2)) << 4);
+        if ((n & 3) != e || l > N) continue;
+        const int8_t* wl = qs ? dt.wbq[N][l] : dt.wb[l];
+        for (int b = 0; b < 16; ++b) {
+          const int dd = 16 * half + b;
+          int v = 0;
+          if (l == N) v = dd == 23 ? 1 : 0;
+          else if (dd < 12) v = wl[dd];
+          else if (dd < 23) v = wl[dd - 11];
+          dst[b] = (uint8_t)(v & 255);
+        }
+      }
+    }
+  return out;
+}
+
 int upload_tables_current_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
@@ -1449,6 +1473,9 @@ int upload_tables_current_device() {
   static DevTables dt;
   make_dev_tables(t, &dt);
   if (cudaMemcpyToSymbol(c_tab, &dt, sizeof(dt)) != cudaSuccess) return 2;
+  static std::vector<uint8_t> wts;
+  if (wts.empty()) wts = make_prep_weight_images(dt);
+  if (cudaMemcpyToSymbol(g_prep_wts, wts.data(), wts.size()) != cudaSuccess) return 2;
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   g_sms[dev] = sms > 0 ? sms : 148;
