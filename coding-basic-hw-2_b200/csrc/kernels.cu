@@ -115,7 +115,8 @@ struct PrepSmem {
   double b[8][32];
   double rowmax[32];
   int sh[32], sg[32];
-  uint64_t bar[2][2];  // [half][buffer]
+  uint64_t bar[2][2];    // [half][buffer]: MMAs of a round complete
+  uint64_t ready[2][2];  // [half][buffer]: the half's 4 warps wrote the round's slots
   uint32_t tmem;
   int abort;
   int issued[2], waited[2];  // per half: rounds whose MMAs were issued / seen complete
@@ -133,11 +134,6 @@ __host__ __device__ constexpr int prep_acc_stride(int n_cols) {
 template <bool kBias>
 __device__ __forceinline__ uint32_t prep_region(int n_cols, int half, int bf) {
   return kBias ? (uint32_t)(half * 128) : (uint32_t)((2 * half + bf) * prep_acc_stride(n_cols));
-}
-// Barrier of the 128 threads of one half (ids 1 and 2; 0 is __syncthreads).
-__device__ __forceinline__ void half_sync(int half) {
-  if (half) asm volatile("bar.sync 2, 128;" ::: "memory");
-  else asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
 // Abs-plane value floor(2^sg |a|) in [0, 127] (0 for an all-zero row).  2^sg |a| < 128 for
@@ -240,6 +236,41 @@ __device__ __forceinline__ bool prep_wait(PrepSmem& sm, int half, int bf, uint32
   return false;
 }
 
+// Barrier of the 128 threads of one half (ids 1 and 2; 0 is __syncthreads).
+__device__ __forceinline__ void half_sync(int half) {
+  if (half) asm volatile("bar.sync 2, 128;" ::: "memory");
+  else asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// Bounded wait of the issuing thread of a half for the 4 warps' arrivals of round i.
+__device__ __forceinline__ bool prep_wait_ready(PrepSmem& sm, int half, int i, DevCounters* cnt) {
+  uint64_t* b = &sm.ready[half][i & 1];
+  const uint32_t parity = (uint32_t)(i >> 1) & 1u;
+  if (mbar_try_wait(b, parity) || mbar_wait(b, parity, global_timer_ns() + 4000000000ull, &sm.abort))
+    return true;
+  sm.abort = 1;
+  atomicCAS(&cnt->status, 0u, (unsigned)kStatusPrepTimeout);
+  return false;
+}
+
+// Issues round i's MMAs of a half (one thread), committed to bar[half][i & 1].
+template <bool kBias>
+__device__ __forceinline__ void prep_issue(PrepSmem& sm, uint32_t tmem, int n_cols, int half,
+                                           int i) {
+  const int bf = i & 1;
+  const uint32_t idesc = idesc_i8(128, n_cols);
+  const uint32_t wb = smem_addr(sm.wts);
+  const uint32_t ab = smem_addr(sm.adig[half][bf]);
+  const uint32_t d = tmem + prep_region<kBias>(n_cols, half, bf);
+  const uint32_t acc0 = kBias ? 1u : 0u;  // biased accumulators add to their start value
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    mma_i8(d, smem_desc_sw32(ab + e * 16 * 256, 256),
+           smem_desc_sw32(wb + e * (n_cols / 8) * 256, 256), idesc, e > 0 ? 1u : acc0);
+  mma_commit(&sm.bar[half][bf]);
+  ++sm.issued[half];
+}
+
 // Second half of round i of this thread's half (its slots are written to buffer i & 1): issues
 // round i's MMAs (thread 0 of the half, committed to bar[half][i & 1]) and turns round i - 1's
 // accumulators into residue bytes (epi(col), col = their TMEM column; when prev).  Returns
@@ -257,23 +288,25 @@ __device__ __forceinline__ bool prep_round(PrepSmem& sm, uint32_t tmem, int n_co
     prep_bias_acc(tmem + prep_region<kBias>(n_cols, half, 0), n_cols);
   }
   if (!dbuf) tmem_st_wait();  // this thread's accumulator reset precedes the MMAs
+  // slots of round i written and the accumulator the MMAs overwrite read.  Single-buffered
+  // (kBias): each warp arrives on ready[half][i & 1] and only the issuing thread waits, so the
+  // warps of a half are not held in lock step (measured faster there); double-buffered: a
+  // barrier of the half (measured faster there: fewer registers live across the round).
   tc_fence_before();
-  half_sync(half);  // slots of round i written; accumulators to be overwritten are read
-  tc_fence_after();
-  if (sm.abort) return false;
-  if ((threadIdx.x & 127) == 0) {
-    const int bf = i & 1;
-    const uint32_t idesc = idesc_i8(128, n_cols);
-    const uint32_t wb = smem_addr(sm.wts);
-    const uint32_t ab = smem_addr(sm.adig[half][bf]);
-    const uint32_t d = tmem + prep_region<kBias>(n_cols, half, bf);
-    const uint32_t acc0 = dbuf ? 0u : 1u;  // biased accumulators add to their start value
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      mma_i8(d, smem_desc_sw32(ab + e * 16 * 256, 256),
-             smem_desc_sw32(wb + e * (n_cols / 8) * 256, 256), idesc, e > 0 ? 1u : acc0);
-    mma_commit(&sm.bar[half][bf]);
-    ++sm.issued[half];
+  if constexpr (kBias) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.ready[half][i & 1]);
+    if ((threadIdx.x & 127) == 0 && prep_wait_ready(sm, half, i, cnt)) {
+      tc_fence_after();
+      prep_issue<kBias>(sm, tmem, n_cols, half, i);
+    }
+    __syncwarp();
+    if (sm.abort) return false;
+  } else {
+    half_sync(half);
+    tc_fence_after();
+    if (sm.abort) return false;
+    if ((threadIdx.x & 127) == 0) prep_issue<kBias>(sm, tmem, n_cols, half, i);
   }
   if (dbuf && prev && prep_wait(sm, half, pb, pp, cnt)) epi(prep_region<kBias>(n_cols, half, pb));
   return true;
@@ -638,6 +671,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     for (int h = 0; h < 2; ++h) {
       mbar_init(&sm.bar[h][0], 1);
       mbar_init(&sm.bar[h][1], 1);
+      mbar_init(&sm.ready[h][0], 4);
+      mbar_init(&sm.ready[h][1], 4);
       sm.issued[h] = 0;
       sm.waited[h] = 0;
     }
