@@ -630,26 +630,34 @@ __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters
   }
 }
 
-template <typename P>
-__device__ __forceinline__ int find_owner(const P* __restrict__ prefix, int num, P x) {
-  int lo = 0, hi = num - 1;  // largest i with prefix[i] <= x
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (prefix[mid] <= x) lo = mid;
-    else hi = mid - 1;
-  }
-  return lo;
-}
-
-// find_owner by one warp (every warp of a block computes the same value): lane L counts the
-// entries i = L (mod 32) with prefix[i] <= x, eight loads in flight at a time (one memory round
-// trip per 256 entries instead of one per bisection step).  Call by all 32 lanes.
+// Owner of x in an exclusive prefix array (prefix[0] = 0 <= x, non-decreasing): the largest
+// i < num with prefix[i] <= x.  Found by one warp (every warp of a block computes the same
+// value): up to 256 entries, lane L counts the
+// entries i = L (mod 32) with prefix[i] <= x, all loads in flight at once (one memory round trip
+// instead of one per bisection step).  Above 256 entries, a 32-way search: each round the lanes
+// probe 32 evenly spaced entries of the remaining range (ceil(log32 num) round trips).  Call by
+// all 32 lanes.
 template <typename P>
 __device__ __forceinline__ int find_owner_warp(const P* __restrict__ prefix, int num, P x) {
-  int c = 0;
-#pragma unroll 8
-  for (int i = threadIdx.x & 31; i < num; i += 32) c += prefix[i] <= x ? 1 : 0;
-  return __reduce_add_sync(0xFFFFFFFFu, c) - 1;
+  const int lane = threadIdx.x & 31;
+  if (num <= 256) {
+    int c = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = lane + 32 * k;
+      c += (i < num && prefix[i] <= x) ? 1 : 0;
+    }
+    return __reduce_add_sync(0xFFFFFFFFu, c) - 1;
+  }
+  int lo = 0, hi = num;  // prefix[lo] <= x; the answer lies in [lo, hi)
+  while (hi - lo > 1) {
+    const int step = (hi - lo + 31) >> 5;
+    const int pos = lo + lane * step;
+    const unsigned ok = __ballot_sync(0xFFFFFFFFu, pos < hi && prefix[pos] <= x);
+    lo += (31 - __clz(ok)) * step;  // lane 0 probes lo itself, so ok != 0
+    hi = min(hi, lo + step);
+  }
+  return lo;
 }
 
 // Compiled twice: kBias = false for descriptors with N <= 15, true for N > 15 (the host
@@ -741,18 +749,21 @@ struct TileInfo {
   int plane, tm, tn;
 };
 
+// Tile t of the call: its job (warp-parallel owner search, so call by all 32 lanes), plane and
+// tile coordinates (a job has fewer than 2^31 tiles).
 __device__ __forceinline__ TileInfo decode_tile(const GemmJob* __restrict__ jobs,
                                                 const long long* __restrict__ prefix, int num,
                                                 long long t) {
   TileInfo ti;
-  const int j = find_owner(prefix, num, t);
+  const int j = find_owner_warp(prefix, num, t);
   ti.job = jobs + j;
-  const long long local = t - prefix[j];
-  const int per_plane = ti.job->tm * ti.job->tn;
-  ti.plane = (int)(local / per_plane);
-  const int rem = (int)(local - (long long)ti.plane * per_plane);
-  ti.tn = rem / ti.job->tm;
-  ti.tm = rem - ti.tn * ti.job->tm;
+  const int local = (int)(t - prefix[j]);
+  const int tm = ti.job->tm;
+  const int per_plane = tm * ti.job->tn;
+  ti.plane = local / per_plane;
+  const int rem = local - ti.plane * per_plane;
+  ti.tn = rem / tm;
+  ti.tm = rem - ti.tn * tm;
   return ti;
 }
 
@@ -902,7 +913,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     uint32_t armed = 0, last_par = 0;  // per stage: ever armed / parity of the last arming
-    for (long long t = blockIdx.x; t < total_tiles && !ctl->abort; t += gridDim.x) {
+    // the abort flag is read warp-uniformly (the tile decode is a warp collective)
+    for (long long t = blockIdx.x;
+         t < total_tiles && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort);
+         t += gridDim.x) {
       const TileInfo ti = decode_tile(jobs, prefix, num, t);
       const GemmJob& jb = *ti.job;
       const int g0a = ti.tm * 16, ga = min(16, jb.rga - g0a);
@@ -947,53 +961,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_wait(&ctl->full[s], (last_par >> s) & 1u, deadline, &dummy_abort);
         }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc128 = idesc_i8(kGemmBM, 128), idesc256 = idesc_i8(kGemmBM, 256);
-      int stage = 0;
-      uint32_t phase = 0;
-      int buf = 0;
-      uint32_t acc_phase = 0;
-      bool issued = false;
-      for (long long t = blockIdx.x; t < total_tiles && !ctl->abort; t += gridDim.x) {
-        const TileInfo ti = decode_tile(jobs, prefix, num, t);
-        const int ksteps = ti.job->ksteps;
-        const uint32_t idesc = ti.job->bn == 256 ? idesc256 : idesc128;
-        if (!bounded_wait(&ctl->acc_empty[buf], acc_phase ^ 1u, ctl, cnt)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem + (uint32_t)(buf * kGemmBNMax);
-        bool ok = true;
-        for (int ks = 0; ks < ksteps; ks += 4) {
-          const int nst = min(4, ksteps - ks);
-          if (!bounded_wait(&ctl->full[stage], phase, ctl, cnt)) { ok = false; break; }
+    // ------------------------------------------------------------------ MMA issuer
+    // The whole warp walks the tiles (the tile decode is warp-parallel); lane 0 waits and issues.
+    constexpr uint32_t idesc128 = idesc_i8(kGemmBM, 128), idesc256 = idesc_i8(kGemmBM, 256);
+    int stage = 0;
+    uint32_t phase = 0;
+    int buf = 0;
+    uint32_t acc_phase = 0;
+    bool issued = false;
+    // the abort flag is read warp-uniformly (the tile decode is a warp collective)
+    for (long long t = blockIdx.x;
+         t < total_tiles && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort);
+         t += gridDim.x) {
+      const TileInfo ti = decode_tile(jobs, prefix, num, t);
+      const int ksteps = ti.job->ksteps;
+      const uint32_t idesc = ti.job->bn == 256 ? idesc256 : idesc128;
+      bool ok = true;
+      if (lane == 0) {
+        ok = bounded_wait(&ctl->acc_empty[buf], acc_phase ^ 1u, ctl, cnt);
+        if (ok) {
           tc_fence_after();
-          const uint32_t sa = smem_addr(smem + stage * kStageBytes);
-          const uint32_t sb = sa + 4 * kStepBytesA;
-          for (int j = 0; j < nst; ++j) {
-            const uint64_t ad = smem_desc_sw32(sa + j * kStepBytesA, 256);
-            const uint64_t bd = smem_desc_sw32(sb + j * kStepBytesB, 256);
-            mma_i8(d_tmem, ad, bd, idesc, (ks > 0 || j > 0) ? 1u : 0u);
+          const uint32_t d_tmem = tmem + (uint32_t)(buf * kGemmBNMax);
+          for (int ks = 0; ks < ksteps; ks += 4) {
+            const int nst = min(4, ksteps - ks);
+            if (!bounded_wait(&ctl->full[stage], phase, ctl, cnt)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = smem_addr(smem + stage * kStageBytes);
+            const uint32_t sb = sa + 4 * kStepBytesA;
+            for (int j = 0; j < nst; ++j) {
+              const uint64_t ad = smem_desc_sw32(sa + j * kStepBytesA, 256);
+              const uint64_t bd = smem_desc_sw32(sb + j * kStepBytesB, 256);
+              mma_i8(d_tmem, ad, bd, idesc, (ks > 0 || j > 0) ? 1u : 0u);
+            }
+            issued = true;
+            mma_commit(&ctl->empty[stage]);
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
-          issued = true;
-          mma_commit(&ctl->empty[stage]);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (!ok) break;
-        mma_commit(&ctl->acc_full[buf]);
-        if (++buf == 2) {
-          buf = 0;
-          acc_phase ^= 1u;
+          if (ok) mma_commit(&ctl->acc_full[buf]);
         }
       }
-      if (issued) {  // all MMAs of this CTA complete before TMEM is released
-        mma_commit(&ctl->drain);
-        const uint64_t deadline = global_timer_ns() + kWaitNs;
-        int dummy_abort = 0;
-        mbar_wait(&ctl->drain, 0, deadline, &dummy_abort);
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+      if (++buf == 2) {
+        buf = 0;
+        acc_phase ^= 1u;
       }
+    }
+    if (lane == 0 && issued) {  // all MMAs of this CTA complete before TMEM is released
+      mma_commit(&ctl->drain);
+      const uint64_t deadline = global_timer_ns() + kWaitNs;
+      int dummy_abort = 0;
+      mbar_wait(&ctl->drain, 0, deadline, &dummy_abort);
     }
   } else {
     // ------------------------------------------------------------------- epilogue
