@@ -749,6 +749,42 @@ struct TileInfo {
   int plane, tm, tn;
 };
 
+// Order in which CTA b walks the tiles (all three roles walk the same order).  The host sorts
+// the jobs by tile cost (deepest K first), so the first half of the tile numbering holds the
+// heavy tiles and the second half the light ones; CTA b alternates between a front walk
+// (tiles t < T/2 with t = b mod G, heaviest first) and a back walk (tiles t >= T/2 with
+// T - 1 - t = b mod G, lightest first), so that the epilogue of a light tile overlaps the MMAs of
+// a heavy one.  Every tile is visited by exactly one CTA.
+struct TileWalk {
+  long long T, nf, nb;
+  int b, G;
+  __device__ __forceinline__ long long count() const { return nf + nb; }
+  __device__ __forceinline__ long long at(long long i) const {
+    const long long m = nf < nb ? nf : nb;
+    bool front;
+    long long k;
+    if (i < 2 * m) {
+      front = (i & 1) == 0;
+      k = i >> 1;
+    } else {
+      front = nf > nb;
+      k = m + (i - 2 * m);
+    }
+    return front ? b + k * G : T - 1 - b - k * G;
+  }
+};
+
+__device__ __forceinline__ TileWalk tile_walk(long long T) {
+  TileWalk w;
+  w.T = T;
+  w.b = (int)blockIdx.x;
+  w.G = (int)gridDim.x;
+  const long long mid = T / 2;
+  w.nf = mid > w.b ? (mid - 1 - w.b) / w.G + 1 : 0;
+  w.nb = T - 1 - w.b >= mid ? (T - 1 - w.b - mid) / w.G + 1 : 0;
+  return w;
+}
+
 // Tile t of the call: its job (warp-parallel owner search, so call by all 32 lanes), plane and
 // tile coordinates (a job has fewer than 2^31 tiles).
 __device__ __forceinline__ TileInfo decode_tile(const GemmJob* __restrict__ jobs,
@@ -905,6 +941,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
+  const TileWalk walk = tile_walk(total_tiles);
 
   if (warp == 0) {
     // --------------------------------------------------------------------- producer
@@ -914,10 +951,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t phase = 0;
     uint32_t armed = 0, last_par = 0;  // per stage: ever armed / parity of the last arming
     // the abort flag is read warp-uniformly (the tile decode is a warp collective)
-    for (long long t = blockIdx.x;
-         t < total_tiles && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort);
-         t += gridDim.x) {
-      const TileInfo ti = decode_tile(jobs, prefix, num, t);
+    for (long long it = 0;
+         it < walk.count() && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort); ++it) {
+      const TileInfo ti = decode_tile(jobs, prefix, num, walk.at(it));
       const GemmJob& jb = *ti.job;
       const int g0a = ti.tm * 16, ga = min(16, jb.rga - g0a);
       const int gbt = jb.bn / 8;
@@ -970,10 +1006,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_phase = 0;
     bool issued = false;
     // the abort flag is read warp-uniformly (the tile decode is a warp collective)
-    for (long long t = blockIdx.x;
-         t < total_tiles && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort);
-         t += gridDim.x) {
-      const TileInfo ti = decode_tile(jobs, prefix, num, t);
+    for (long long it = 0;
+         it < walk.count() && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort); ++it) {
+      const TileInfo ti = decode_tile(jobs, prefix, num, walk.at(it));
       const int ksteps = ti.job->ksteps;
       const uint32_t idesc = ti.job->bn == 256 ? idesc256 : idesc128;
       bool ok = true;
@@ -1021,8 +1056,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quad = warp & 3;
     int buf = 0;
     uint32_t acc_phase = 0;
-    for (long long t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = decode_tile(jobs, prefix, num, t);
+    for (long long it = 0; it < walk.count(); ++it) {
+      const TileInfo ti = decode_tile(jobs, prefix, num, walk.at(it));
       const GemmJob& jb = *ti.job;
       bool ok = true;
       if (lane == 0) ok = bounded_wait(&ctl->acc_full[buf], acc_phase, ctl, cnt);
