@@ -729,7 +729,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
 //   32 (w % 4) .. 32 (w % 4) + 31, i.e. tile rows.
 // Two TMEM accumulators (2 x 256 columns, all of TMEM) let the epilogue of one tile overlap the
 // MMAs of the next.  The 256-column tile halves the operand bytes fetched per MAC of the
-// B side, which (with 128 x 128 tiles) bound the kernel by L2 -> SM traffic.  Tiles are handed out statically (tile t to CTA t mod grid) from a host-side LPT order.
+// B side, which (with 128 x 128 tiles) bound the kernel by L2 -> SM traffic.  Tiles come from a
+// host-side LPT order; each CTA walks it from both ends (TileWalk).
 constexpr int kStages = 4;
 constexpr int kStepBytesA = 16 * 256;                     // one 32-byte K step of 128 rows
 constexpr int kStepBytesB = 32 * 256;                     // ... of 256 rows
@@ -999,7 +1000,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     // The whole warp walks the tiles (the tile decode is warp-parallel); lane 0 waits and issues.
-    constexpr uint32_t idesc128 = idesc_i8(kGemmBM, 128), idesc256 = idesc_i8(kGemmBM, 256);
     int stage = 0;
     uint32_t phase = 0;
     int buf = 0;
@@ -1010,7 +1010,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
          it < walk.count() && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort); ++it) {
       const TileInfo ti = decode_tile(jobs, prefix, num, walk.at(it));
       const int ksteps = ti.job->ksteps;
-      const uint32_t idesc = ti.job->bn == 256 ? idesc256 : idesc128;
+      // MMA width: the tile's columns inside the problem, rounded up to 16 (edge tiles of a
+      // ragged n skip the padding columns; the epilogue never reads past the problem's n)
+      const int nrem = ti.job->n - ti.tn * ti.job->bn;
+      const uint32_t idesc = idesc_i8(kGemmBM, min(ti.job->bn, (nrem + 15) & ~15));
       bool ok = true;
       if (lane == 0) {
         ok = bounded_wait(&ctl->acc_empty[buf], acc_phase ^ 1u, ctl, cnt);
