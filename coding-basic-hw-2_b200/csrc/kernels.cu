@@ -743,7 +743,16 @@ struct GemmSmemCtl {
   uint32_t tmem_base;
   int abort;
 };
-constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + sizeof(GemmSmemCtl) + 64;
+// Tile schedule of a CTA in shared memory: {job, plane, tm, tn} of each tile of its walk, built
+// once at kernel start (bisection over the job prefix staged in the still unused operand ring),
+// so that no role decodes a tile on its critical path.  Used when the CTA walks at most
+// kSchedMax tiles and the call has at most kSchedJobs jobs; otherwise every role decodes each
+// tile itself (warp-parallel search).
+constexpr int kSchedMax = 1024;
+constexpr int kSchedJobs = 4096;
+static_assert((kSchedJobs + 1) * 8 <= kStages * kStageBytes, "prefix staging");
+constexpr size_t kGemmSmem =
+    1024 + kStages * kStageBytes + sizeof(GemmSmemCtl) + 64 + kSchedMax * sizeof(int4);
 
 struct TileInfo {
   const GemmJob* job;
@@ -943,6 +952,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
   const TileWalk walk = tile_walk(total_tiles);
+  int4* sched = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(ctl) +
+                                        ((sizeof(GemmSmemCtl) + 63) & ~size_t(63)));
+  const bool cached = walk.count() <= kSchedMax && num <= kSchedJobs;  // block-uniform
+  if (cached) {
+    long long* sp = reinterpret_cast<long long*>(smem);
+    for (int x = threadIdx.x; x < num; x += blockDim.x) sp[x] = prefix[x];
+    __syncthreads();
+    for (int x = threadIdx.x; x < (int)walk.count(); x += blockDim.x) {
+      const long long t = walk.at(x);
+      int lo = 0, hi = num - 1;  // largest j with sp[j] <= t
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (sp[mid] <= t) lo = mid;
+        else hi = mid - 1;
+      }
+      const int local = (int)(t - sp[lo]);
+      const int tm = jobs[lo].tm;
+      const int per_plane = tm * jobs[lo].tn;
+      const int plane = local / per_plane;
+      const int rem = local - plane * per_plane;
+      sched[x] = make_int4(lo, plane, rem - (rem / tm) * tm, rem / tm);
+    }
+    __syncthreads();  // the staged prefix in the operand ring is no longer read
+  }
+  // tile `it` of this CTA's walk (warp-collective when not cached)
+  auto tile_of = [&](long long it) -> TileInfo {
+    if (cached) {
+      const int4 r = sched[it];
+      TileInfo ti;
+      ti.job = jobs + r.x;
+      ti.plane = r.y;
+      ti.tm = r.z;
+      ti.tn = r.w;
+      return ti;
+    }
+    return decode_tile(jobs, prefix, num, walk.at(it));
+  };
 
   if (warp == 0) {
     // --------------------------------------------------------------------- producer
@@ -954,7 +1000,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // the abort flag is read warp-uniformly (the tile decode is a warp collective)
     for (long long it = 0;
          it < walk.count() && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort); ++it) {
-      const TileInfo ti = decode_tile(jobs, prefix, num, walk.at(it));
+      const TileInfo ti = tile_of(it);
       const GemmJob& jb = *ti.job;
       const int g0a = ti.tm * 16, ga = min(16, jb.rga - g0a);
       const int gbt = jb.bn / 8;
@@ -1008,7 +1054,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // the abort flag is read warp-uniformly (the tile decode is a warp collective)
     for (long long it = 0;
          it < walk.count() && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort); ++it) {
-      const TileInfo ti = decode_tile(jobs, prefix, num, walk.at(it));
+      const TileInfo ti = tile_of(it);
       const int ksteps = ti.job->ksteps;
       // MMA width: the tile's columns inside the problem, rounded up to 16 (edge tiles of a
       // ragged n skip the padding columns; the epilogue never reads past the problem's n)
@@ -1060,7 +1106,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int buf = 0;
     uint32_t acc_phase = 0;
     for (long long it = 0; it < walk.count(); ++it) {
-      const TileInfo ti = decode_tile(jobs, prefix, num, walk.at(it));
+      const TileInfo ti = tile_of(it);
       const GemmJob& jb = *ti.job;
       bool ok = true;
       if (lane == 0) ok = bounded_wait(&ctl->acc_full[buf], acc_phase, ctl, cnt);

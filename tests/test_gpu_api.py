@@ -305,6 +305,27 @@ def test_nonfinite_alpha_zero_small_k_auto(g2, cuda):
     assert grp.gate(grp.outputs())[0] == 0
 
 
+def test_group_beyond_cached_tile_schedule(g2, cuda):
+    """More GEMM jobs than the per-CTA tile schedule caches (4096): the GEMM decodes each tile
+    itself.  Same bytes as the group run in two calls below that size."""
+    shapes = [(16 + (i % 5) * 8, 24 + (i % 3) * 8, 40 + (i % 7) * 16) for i in range(4200)]
+    grp = Group(shapes, 1.0, 1.0, 0.5, seed=42)
+    cfg = g2.config(15, 1e-15, 0, 0)
+    rc, _ = run(g2, grp, 3, cfg, stats_env=False)
+    assert rc == 0
+    whole = [c.copy() for c in grp.outputs()]
+    parts = []
+    for lo, hi in ((0, 2100), (2100, 4200)):
+        sub = Group(shapes[lo:hi], 1.0, 1.0, 0.5, seed=0)
+        sub.items = grp.items[lo:hi]
+        sub.reset()
+        rc, _ = run(g2, sub, 3, cfg, stats_env=False)
+        assert rc == 0
+        parts += sub.outputs()
+    for a, b in zip(whole, parts):
+        assert np.array_equal(a.view(np.uint64), b.view(np.uint64))
+
+
 def test_chunked_group_matches_single_pass(g2, cuda):
     """A handle whose workspace holds only a few problems runs the group in chunks, with the
     same bytes as one pass."""
