@@ -872,38 +872,45 @@ __device__ __forceinline__ uint32_t digit_of(uint32_t c, const DigitCtx& dc) {
   return kQ ? crt_digit_q(c, dc) : crt_digit(c, dc);
 }
 
-// One 32-column record of one row: 32 digit bytes (two 16-byte stores) or 32 int32 (eight).
+// 32 columns of one row: two 16-digit records (16 bytes each, at ydst and ydst + dstep) or eight
+// 4-product records (at ldst + g * lstep).  Consecutive rows' records are adjacent, so a warp
+// (32 consecutive rows) writes 512 contiguous bytes per store instruction.
 template <bool kQ>
 __device__ __forceinline__ void emit_record(const uint32_t (&v)[32], const DigitCtx& dc,
-                                            uint8_t* ydst, int32_t* ldst) {
+                                            uint8_t* ydst, long long dstep, int32_t* ldst,
+                                            long long lstep) {
   if (dc.digit) {
     uint32_t w[8];
 #pragma unroll
     for (int g = 0; g < 8; ++g)
       w[g] = digit_of<kQ>(v[4 * g], dc) | (digit_of<kQ>(v[4 * g + 1], dc) << 8) |
              (digit_of<kQ>(v[4 * g + 2], dc) << 16) | (digit_of<kQ>(v[4 * g + 3], dc) << 24);
-    uint4* d = reinterpret_cast<uint4*>(ydst);
-    d[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    *reinterpret_cast<uint4*>(ydst) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(ydst + dstep) = make_uint4(w[4], w[5], w[6], w[7]);
   } else {
-    int4* d = reinterpret_cast<int4*>(ldst);
 #pragma unroll
     for (int g = 0; g < 8; ++g)
-      d[g] = make_int4((int)v[4 * g], (int)v[4 * g + 1], (int)v[4 * g + 2], (int)v[4 * g + 3]);
+      *reinterpret_cast<int4*>(ldst + g * lstep) =
+          make_int4((int)v[4 * g], (int)v[4 * g + 1], (int)v[4 * g + 2], (int)v[4 * g + 3]);
   }
 }
 
-// Digit-layout epilogue of one tile for one thread (TMEM lane = row of the tile): nch records
-// of 32 columns.  kQ: the job's A images are q-scaled (GemmJob::y8 == 2).
+// Digit-layout epilogue of one tile for one thread (TMEM lane = row of the tile): nch chunks of
+// 32 columns.  kQ: the job's A images are q-scaled (GemmJob::y8 == 2).
 template <bool kQ>
 __device__ __forceinline__ void gemm_digit_records(const GemmJob& jb, const TileInfo& ti, int row,
                                                    uint32_t taddr, int nch) {
   const int pl = jb.plane0 + ti.plane;
   const DigitCtx dc = digit_ctx(pl, jb.N, kQ);
-  const long long rec0 = ((long long)ti.tn * (jb.bn / 32) * jb.m + row) * 32;
-  uint8_t* ydst = jb.Y + (long long)pl * jb.y_plane + rec0;
-  int32_t* ldst = reinterpret_cast<int32_t*>(jb.Y + (long long)jb.N * jb.y_plane) + rec0;
-  const long long cstep = (long long)jb.m * 32;  // one record column
+  // digit records of 16 columns, abs records of 4: column j of this row at record j / 16 (j / 4)
+  const long long c0 = (long long)ti.tn * jb.bn;  // the tile's first column
+  uint8_t* ydst = jb.Y + (long long)pl * jb.y_plane + ((c0 / 16) * jb.m + row) * 16;
+  int32_t* ldst = reinterpret_cast<int32_t*>(jb.Y + (long long)jb.N * jb.y_plane) +
+                  ((c0 / 4) * jb.m + row) * 4;
+  const long long dstep = (long long)jb.m * 16;  // next 16-column digit record (bytes)
+  const long long lstep = (long long)jb.m * 4;   // next 4-column abs record (int32)
+  const long long cstep = 2 * dstep;             // 32 columns further (bytes)
+  const long long lcstep = 8 * lstep;            // ... (int32)
   const bool live = row < jb.m;
   // two register buffers: the TMEM load of chunk c + 1 overlaps the digits of chunk c
   uint32_t va[32], vb[32];
@@ -912,11 +919,12 @@ __device__ __forceinline__ void gemm_digit_records(const GemmJob& jb, const Tile
 #pragma unroll 1
   for (int c = 0; c < nch; c += 2) {
     if (c + 1 < nch) tmem_ld_32x32b_x32(taddr + (uint32_t)((c + 1) * 32), vb);
-    if (live) emit_record<kQ>(va, dc, ydst + c * cstep, ldst + c * cstep);
+    if (live) emit_record<kQ>(va, dc, ydst + c * cstep, dstep, ldst + c * lcstep, lstep);
     if (c + 1 < nch) {
       tmem_ld_wait(vb);
       if (c + 2 < nch) tmem_ld_32x32b_x32(taddr + (uint32_t)((c + 2) * 32), va);
-      if (live) emit_record<kQ>(vb, dc, ydst + (c + 1) * cstep, ldst + (c + 1) * cstep);
+      if (live)
+        emit_record<kQ>(vb, dc, ydst + (c + 1) * cstep, dstep, ldst + (c + 1) * lcstep, lstep);
       if (c + 2 < nch) tmem_ld_wait(va);
     }
   }
@@ -1449,16 +1457,18 @@ __device__ __noinline__ void recon_c32_block(const ggemm_recon_desc_t* __restric
 __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long long local,
                                                int mode, unsigned& n_unc, unsigned& n_rep,
                                                unsigned& n_saf) {
-  __shared__ int s_sh[2][32];      // csh, tau of the 32 columns
-  __shared__ double s_nrm[2][32];  // ||dB_j||, ||B'_j|| (float upper bounds, widened once)
+  __shared__ int s_sh[2][16];      // csh, tau of the 16 columns
+  __shared__ double s_nrm[2][16];  // ||dB_j||, ||B'_j|| (float upper bounds, widened once)
+  // block: kY8Rows rows x one 16-column digit record; thread: row i, columns j0 .. j0 + 7 (half
+  // cg of the record).  A warp (16 rows) reads 256 contiguous bytes of a digit plane.
   const bool ok_desc = d.N >= 1 && d.N <= kMaxModuli && d.m > 0 && d.n > 0;
   const long long rblocks = ok_desc ? (d.m + kY8Rows - 1) / kY8Rows : 1;
   const int ch = ok_desc ? (int)(local / rblocks) : 0;
-  const int i = (int)(local - ch * rblocks) * kY8Rows + (threadIdx.x >> 2);
-  const int cg = threadIdx.x & 3;
+  const int i = (int)(local - ch * rblocks) * kY8Rows + (threadIdx.x >> 1);
+  const int cg = threadIdx.x & 1;
   const bool planes = ok_desc && d.alpha != 0.0 && d.k > 0;
-  if (threadIdx.x < 64) {
-    const int st = threadIdx.x >> 5, x = threadIdx.x & 31, j = ch * 32 + x;
+  if (threadIdx.x < 32) {
+    const int st = threadIdx.x >> 4, x = threadIdx.x & 15, j = ch * 16 + x;
     const bool v = ok_desc && d.alpha != 0.0 && j < d.n;
     s_sh[st][x] = v ? d.cs[st * d.n + j] : 0;
     s_nrm[st][x] = v ? (double)__int_as_float(d.cs[(2 + st) * d.n + j]) : 0.0;
@@ -1467,9 +1477,11 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
   if (!ok_desc || i >= d.m) return;
   const ReconCtx cx = recon_ctx(d);
   const int N = cx.N;
-  const int j0 = ch * 32 + cg * 8;
+  const int j0 = ch * 16 + cg * 8;
   const int ncol = min(8, d.n - j0);
-  const long long rec = ((long long)ch * d.m + i) * 32 + cg * 8;
+  // columns j0 .. j0 + 7: half cg of digit record ch, abs records 4 ch + 2 cg and the next one
+  const long long rec = ((long long)ch * d.m + i) * 16 + cg * 8;
+  const long long lrec = ((long long)(4 * ch + 2 * cg) * d.m + i) * 4;
   const uint8_t* Y = reinterpret_cast<const uint8_t*>(d.C32);
   uint2 yv[kMaxModuli];
   int4 l0 = make_int4(0, 0, 0, 0), l1 = l0;
@@ -1477,10 +1489,9 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
 #pragma unroll
     for (int l = 0; l < kMaxModuli; ++l)
       if (l < N) yv[l] = __ldg(reinterpret_cast<const uint2*>(Y + l * d.c_plane + rec));
-    const int4* lp = reinterpret_cast<const int4*>(
-        reinterpret_cast<const int32_t*>(Y + (long long)N * d.c_plane) + rec);
-    l0 = __ldg(lp);
-    l1 = __ldg(lp + 1);
+    const int32_t* lp = reinterpret_cast<const int32_t*>(Y + (long long)N * d.c_plane) + lrec;
+    l0 = __ldg(reinterpret_cast<const int4*>(lp));
+    l1 = __ldg(reinterpret_cast<const int4*>(lp + 4LL * d.m));
   }
   int rsh = 0, sig = 0;
   double da = 0.0, na = 0.0;

@@ -26,8 +26,10 @@ enum : unsigned int {
 };
 
 // Digit layout ("Y8", GGEMM_PRODUCTS_DIGITS in ggemm_stages.h) of the products handed from the
-// GEMM to the reconstruct: an epilogue lane (one row) writes 32 contiguous bytes per digit
-// plane, and a reconstruct thread reads 8 columns of one plane with one 8-byte load.
+// GEMM to the reconstruct: 16-byte records (16 digits, or 4 int32 abs products) of one row,
+// the records of a column block stored row after row, so that a GEMM epilogue warp (32 rows)
+// writes 512 contiguous bytes per store and a reconstruct thread reads 8 columns of one plane
+// with one 8-byte load.  Planes are sized for whole 32-column chunks (the epilogue's unit).
 inline size_t y8_plane_bytes(int m, int n) { return ggemm_digit_plane_bytes(m, n); }
 inline size_t y8_bytes(int m, int n, int N) {
   return (size_t)N * y8_plane_bytes(m, n) + 4 * y8_plane_bytes(m, n);
@@ -75,11 +77,11 @@ inline long long recon_blocks(const ggemm_recon_desc_t& d) {
   const long long per = (long long)kReconThreads * kReconPerThread;
   return (mn + per - 1) / per;
 }
-// Digit-layout reconstruct: one block per 64 rows x 32 columns (one record column).
-constexpr int kY8Rows = 64;
+// Digit-layout reconstruct: one block per 128 rows x 16 columns (one digit record column).
+constexpr int kY8Rows = 128;
 inline long long recon_blocks_y8(const ggemm_recon_desc_t& d) {
   if (d.m <= 0 || d.n <= 0) return 0;
-  return (long long)((d.n + 31) / 32) * ((d.m + kY8Rows - 1) / kY8Rows);
+  return (long long)((d.n + 15) / 16) * ((d.m + kY8Rows - 1) / kY8Rows);
 }
 // Blocks of one reconstruct descriptor in its layout.
 inline long long recon_job_blocks(const ggemm_recon_desc_t& d) {

@@ -69,11 +69,14 @@ typedef struct {
  *   (ld = m), at stride c_plane int32 elements.
  * GGEMM_PRODUCTS_DIGITS: for residue plane l < N the CRT digit y_l = (C_l mod p_l) q_l mod p_l
  *   (the value the reconstruct derives from C_l first) as one byte; for the abs plane l = N
- *   the int32 product.  Both in records of 32 consecutive columns of one row, c_plane in bytes:
- *     digit y_l(i, j):   byte  at base + l*c_plane + ((j/32)*m + i)*32 + j%32
- *     abs product (i, j): int32 at ((int32_t*)(base + N*c_plane))[((j/32)*m + i)*32 + j%32]
+ *   the int32 product.  Both in 16-byte records of consecutive columns of one row (16 digits,
+ *   or 4 int32 products), the records of one column block stored row after row, c_plane in
+ *   bytes:
+ *     digit y_l(i, j):   byte  at base + l*c_plane + ((j/16)*m + i)*16 + j%16
+ *     abs product (i, j): int32 at ((int32_t*)(base + N*c_plane))[((j/4)*m + i)*4 + j%4]
  *   c_plane >= ggemm_digit_plane_bytes(m, n) and a multiple of 16; the abs plane takes
- *   4 * ggemm_digit_plane_bytes(m, n) bytes.  Columns j >= n of the last record are padding.
+ *   4 * ggemm_digit_plane_bytes(m, n) bytes.  Columns j >= n, up to the next multiple of 32,
+ *   are padding (the GEMM writes whole 32-column chunks).
  *   N + 4 bytes per entry instead of 4 (N + 1). */
 #define GGEMM_PRODUCTS_INT32 0
 #define GGEMM_PRODUCTS_DIGITS 1

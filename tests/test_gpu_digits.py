@@ -43,21 +43,29 @@ def digits_of(C: np.ndarray, N: int, t) -> np.ndarray:
     return (C[:N] % p) * q % p
 
 
+def records_of(M: np.ndarray, m: int, n: int, w: int) -> np.ndarray:
+    """(m, n) matrix -> its records of w columns of one row, the records of a column block row
+    after row (the digit layout: w = 16 digit bytes or w = 4 int32 abs products), padded with
+    zeros to whole 32-column chunks."""
+    nrec = (n + 31) // 32 * (32 // w)
+    pad = np.zeros((m, nrec * w), dtype=M.dtype)
+    pad[:, :n] = M
+    return pad.reshape(m, nrec, w).transpose(1, 0, 2).reshape(-1)
+
+
 def to_records(Y: np.ndarray, m: int, n: int, yp: int, N: int) -> np.ndarray:
-    """(N, m, n) digits + nothing else -> the digit planes of the layout (padding zero)."""
-    nch = (n + 31) // 32
+    """(N, m, n) digits -> the digit planes of the layout (padding zero)."""
     out = np.zeros((N, yp), dtype=np.uint8)
     for l in range(N):
-        pad = np.zeros((m, nch * 32), dtype=np.uint8)
-        pad[:, :n] = Y[l]
-        out[l, :nch * m * 32] = pad.reshape(m, nch, 32).transpose(1, 0, 2).reshape(-1)
+        r = records_of(Y[l], m, n, 16)
+        out[l, :r.size] = r
     return out
 
 
-def from_records(buf: np.ndarray, m: int, n: int) -> np.ndarray:
-    """One plane of 32-column records -> its (m, n) matrix (padding columns dropped)."""
-    nch = (n + 31) // 32
-    return buf[:nch * m * 32].reshape(nch, m, 32).transpose(1, 0, 2).reshape(m, nch * 32)[:, :n]
+def from_records(buf: np.ndarray, m: int, n: int, w: int = 16) -> np.ndarray:
+    """One plane of w-column records -> its (m, n) matrix (padding columns dropped)."""
+    nrec = (n + 31) // 32 * (32 // w)
+    return buf[:nrec * m * w].reshape(nrec, m, w).transpose(1, 0, 2).reshape(m, nrec * w)[:, :n]
 
 
 def _rand_planes(rng, P, rows, k, lo=-128, hi=128):
@@ -98,7 +106,7 @@ def run_gemm_digits(g2, A8s, B8s, ks, Ns, layout=None):
     for dy, m, n, N, yp in outs:
         h = dy.cpu().numpy()
         Y = np.stack([from_records(h[l * yp:(l + 1) * yp], m, n) for l in range(N)])
-        L = from_records(h[N * yp:].view(np.int32), m, n)
+        L = from_records(h[N * yp:].view(np.int32), m, n, 4)
         res.append((Y, L))
     return res
 
@@ -209,10 +217,8 @@ def test_recon_digits_matches_oracle(g2, oracle, cuda, tables, mode, m, n, k, N,
     buf = np.zeros(N * yp + 4 * yp, dtype=np.uint8)
     buf[:N * yp] = to_records(digits_of(C, N, tables).astype(np.uint8), m, n, yp, N).reshape(-1)
     Lrec = np.zeros(yp, dtype=np.int32)
-    nch = (n + 31) // 32
-    pad = np.zeros((m, nch * 32), dtype=np.int32)
-    pad[:, :n] = C[N]
-    Lrec[:nch * m * 32] = pad.reshape(m, nch, 32).transpose(1, 0, 2).reshape(-1)
+    r = records_of(C[N].astype(np.int32), m, n, 4)
+    Lrec[:r.size] = r
     buf[N * yp:] = Lrec.view(np.uint8)
     dA, dB = torch.from_numpy(Af).cuda(), torch.from_numpy(Bf).cuda()
     dC = torch.from_numpy(Cf.copy()).cuda()
