@@ -725,12 +725,13 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
 // Warp roles:
 //   warp 0: TMEM allocation + bulk-copy producer (lanes 0-3 copy A, 4-7 copy B)
 //   warp 1: tcgen05.mma issuer (one lane)
-//   warps 2..5: epilogue (TMEM -> registers -> int32 stores); warp w reads TMEM lanes
-//   32 (w % 4) .. 32 (w % 4) + 31, i.e. tile rows.
+//   warps 2..5: epilogue (TMEM -> registers -> CRT digit bytes and int32 abs products, or int32
+//   products); warp w reads TMEM lanes 32 (w % 4) .. 32 (w % 4) + 31, i.e. tile rows.
 // Two TMEM accumulators (2 x 256 columns, all of TMEM) let the epilogue of one tile overlap the
 // MMAs of the next.  The 256-column tile halves the operand bytes fetched per MAC of the
 // B side, which (with 128 x 128 tiles) bound the kernel by L2 -> SM traffic.  Tiles come from a
-// host-side LPT order; each CTA walks it from both ends (TileWalk).
+// host-side LPT order; each CTA walks it from both ends (TileWalk) and keeps its walk's tile
+// coordinates in shared memory (the schedule below).
 constexpr int kStages = 4;
 constexpr int kStepBytesA = 16 * 256;                     // one 32-byte K step of 128 rows
 constexpr int kStepBytesB = 32 * 256;                     // ... of 256 rows
