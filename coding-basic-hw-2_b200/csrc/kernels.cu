@@ -723,7 +723,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
 // ============================================================================== GEMM kernel
 // Tile 128 x 256 (128 x 128 for n <= 128) x (4 x 32-byte K steps) per pipeline stage.
 // Warp roles:
-//   warp 0: TMEM allocation + bulk-copy producer (lanes 0-3 copy A, 4-7 copy B)
+//   warp 0: TMEM allocation + bulk-copy producer (lanes [0, kKS) copy A, [kKS, 2 kKS) copy B)
 //   warp 1: tcgen05.mma issuer (one lane)
 //   warps 2..5: epilogue (TMEM -> registers -> CRT digit bytes and int32 abs products, or int32
 //   products); warp w reads TMEM lanes 32 (w % 4) .. 32 (w % 4) + 31, i.e. tile rows.
@@ -732,10 +732,11 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
 // B side, which (with 128 x 128 tiles) bound the kernel by L2 -> SM traffic.  Tiles come from a
 // host-side LPT order; each CTA walks it from both ends (TileWalk) and keeps its walk's tile
 // coordinates in shared memory (the schedule below).
-constexpr int kStages = 4;
+constexpr int kKS = 4;     // 32-byte K steps per pipeline stage
+constexpr int kStages = 4;  // kStages * kKS * 12 KB of operands in flight
 constexpr int kStepBytesA = 16 * 256;                     // one 32-byte K step of 128 rows
 constexpr int kStepBytesB = 32 * 256;                     // ... of 256 rows
-constexpr int kStageBytes = 4 * (kStepBytesA + kStepBytesB);  // 4 K steps of A and B
+constexpr int kStageBytes = kKS * (kStepBytesA + kStepBytesB);  // kKS K steps of A and B
 constexpr int kGemmThreads = 192;
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
 
@@ -1001,8 +1002,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     // --------------------------------------------------------------------- producer
-    // Lane 0 waits for a free stage and arms its barrier; lanes 0-3 then copy the 4 K steps of
-    // A and lanes 4-7 those of B (parallel issue of the bulk copies).
+    // Lane 0 waits for a free stage and arms its barrier; lanes [0, kKS) then copy the stage's K
+    // steps of A and lanes [kKS, 2 kKS) those of B (parallel issue of the bulk copies).
     int stage = 0;
     uint32_t phase = 0;
     uint32_t armed = 0, last_par = 0;  // per stage: ever armed / parity of the last arming
@@ -1018,8 +1019,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int8_t* B = jb.B + (long long)ti.plane * jb.b_plane + (long long)g0b * 256;
       const long long astep = (long long)jb.rga * 256, bstep = (long long)jb.rgb * 256;
       bool ok = true;
-      for (int ks = 0; ks < jb.ksteps; ks += 4) {
-        const int nst = min(4, jb.ksteps - ks);
+      for (int ks = 0; ks < jb.ksteps; ks += kKS) {
+        const int nst = min(kKS, jb.ksteps - ks);
         if (lane == 0) {
           ok = bounded_wait(&ctl->empty[stage], phase ^ 1u, ctl, cnt);
           if (ok) mbar_arrive_expect_tx(&ctl->full[stage], (uint32_t)(nst * (ga + gb) * 256));
@@ -1029,12 +1030,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         armed |= 1u << stage;
         last_par = (last_par & ~(1u << stage)) | (phase << stage);
         uint8_t* sa = smem + stage * kStageBytes;
-        uint8_t* sb = sa + 4 * kStepBytesA;
+        uint8_t* sb = sa + kKS * kStepBytesA;
         if (lane < nst)
           bulk_g2s(sa + lane * kStepBytesA, A + (long long)(ks + lane) * astep,
                    (uint32_t)(ga * 256), &ctl->full[stage]);
-        else if (lane >= 4 && lane < 4 + nst)
-          bulk_g2s(sb + (lane - 4) * kStepBytesB, B + (long long)(ks + lane - 4) * bstep,
+        else if (lane >= kKS && lane < kKS + nst)
+          bulk_g2s(sb + (lane - kKS) * kStepBytesB, B + (long long)(ks + lane - kKS) * bstep,
                    (uint32_t)(gb * 256), &ctl->full[stage]);
         __syncwarp();
         if (++stage == kStages) {
@@ -1075,12 +1076,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (ok) {
           tc_fence_after();
           const uint32_t d_tmem = tmem + (uint32_t)(buf * kGemmBNMax);
-          for (int ks = 0; ks < ksteps; ks += 4) {
-            const int nst = min(4, ksteps - ks);
+          for (int ks = 0; ks < ksteps; ks += kKS) {
+            const int nst = min(kKS, ksteps - ks);
             if (!bounded_wait(&ctl->full[stage], phase, ctl, cnt)) { ok = false; break; }
             tc_fence_after();
             const uint32_t sa = smem_addr(smem + stage * kStageBytes);
-            const uint32_t sb = sa + 4 * kStepBytesA;
+            const uint32_t sb = sa + kKS * kStepBytesA;
             for (int j = 0; j < nst; ++j) {
               const uint64_t ad = smem_desc_sw32(sa + j * kStepBytesA, 256);
               const uint64_t bd = smem_desc_sw32(sb + j * kStepBytesB, 256);
@@ -1568,15 +1569,18 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
 }
 
 // One launch over every problem of a call; the layout is chosen per problem (block-uniform).
+// Compiled once per repair mode (GGEMM_STAGE_REPAIR_*), so the digit-layout body carries only
+// its mode's certificate / repair branches.
+template <int kMode>
 __global__ void __launch_bounds__(kReconThreads, 2)
     recon_kernel(const ggemm_recon_desc_t* __restrict__ descs,
-                 const long long* __restrict__ prefix, int num, int mode, DevCounters* cnt) {
+                 const long long* __restrict__ prefix, int num, DevCounters* cnt) {
   const int owner = find_owner_warp(prefix, num, (long long)blockIdx.x);
   const ggemm_recon_desc_t d = descs[owner];
   const long long local = (long long)blockIdx.x - prefix[owner];
   unsigned n_unc = 0, n_rep = 0, n_saf = 0;
-  if (d.layout == GGEMM_PRODUCTS_DIGITS) recon_y8_block(d, local, mode, n_unc, n_rep, n_saf);
-  else recon_c32_block(descs + owner, local, mode, n_unc, n_rep, n_saf);
+  if (d.layout == GGEMM_PRODUCTS_DIGITS) recon_y8_block(d, local, kMode, n_unc, n_rep, n_saf);
+  else recon_c32_block(descs + owner, local, kMode, n_unc, n_rep, n_saf);
   flush_counters(n_unc, n_rep, n_saf, cnt);
 }
 
@@ -1684,8 +1688,21 @@ int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix, i
                  long long total_blocks, int mode, DevCounters* cnt, cudaStream_t s) {
   if (num <= 0 || total_blocks <= 0) return 0;
   if (total_blocks > 0x7FFFFFFFLL) return (int)cudaErrorInvalidConfiguration;
-  recon_kernel<<<(unsigned)total_blocks, kReconThreads, 0, s>>>(d_descs, d_prefix, num, mode,
-                                                                cnt);
+  const unsigned grid = (unsigned)total_blocks;
+  switch (mode) {
+    case GGEMM_STAGE_REPAIR_OFF:
+      recon_kernel<GGEMM_STAGE_REPAIR_OFF><<<grid, kReconThreads, 0, s>>>(d_descs, d_prefix, num,
+                                                                          cnt);
+      break;
+    case GGEMM_STAGE_REPAIR_COUNT:
+      recon_kernel<GGEMM_STAGE_REPAIR_COUNT><<<grid, kReconThreads, 0, s>>>(d_descs, d_prefix,
+                                                                            num, cnt);
+      break;
+    default:
+      recon_kernel<GGEMM_STAGE_REPAIR_ON><<<grid, kReconThreads, 0, s>>>(d_descs, d_prefix, num,
+                                                                         cnt);
+      break;
+  }
   return (int)cudaGetLastError();
 }
 
