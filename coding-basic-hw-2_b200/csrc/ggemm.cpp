@@ -346,20 +346,9 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         ++q;
       }
     }
-    // descriptors with N <= 15 first: prep is compiled once per case (launch_prep)
-    std::stable_partition(pd, pd + q,
-                          [](const ggemm_prep_desc_t& d) { return !prep_needs_bias(d.N); });
-    ch.num_prep_lo = 0;
-    ch.prep_blocks_lo = 0;
-    for (int x = 0; x < q; ++x) {
-      pp[x] = blocks;
-      if (!prep_needs_bias(pd[x].N)) {
-        ++ch.num_prep_lo;
-        ch.prep_blocks_lo = blocks + prep_blocks(pd[x]);
-      }
-      blocks += prep_blocks(pd[x]);
-    }
-    pp[q] = blocks;
+    // descriptors sorted by prep instance (launch_prep)
+    prep_partition(pd, q, pp, &ch.prep_split);
+    blocks = (int)ch.prep_split.block0[kPrepClasses];
     ch.prep_blocks = blocks;
 
     // residue GEMM jobs: one per problem (EMU_LOOP: one per plane), heaviest tiles first
@@ -526,9 +515,8 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
     if (!mark(0)) return GGEMM_ERR_CUDA;
     if (ch.prep_blocks > 0) {
       if (launch_prep(reinterpret_cast<const ggemm_prep_desc_t*>(db + ch.off_prep),
-                      reinterpret_cast<const int*>(db + ch.off_prep_prefix), ch.num_prep,
-                      ch.num_prep_lo, ch.prep_blocks_lo, ch.prep_blocks, h->counters, s,
-                      launches))
+                      reinterpret_cast<const int*>(db + ch.off_prep_prefix), ch.prep_split,
+                      h->counters, s, launches))
         return GGEMM_ERR_NUMERICS;
     }
     if (!mark(1)) return GGEMM_ERR_CUDA;

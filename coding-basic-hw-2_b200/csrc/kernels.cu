@@ -367,6 +367,22 @@ __device__ __noinline__ void prep_epilogue(uint32_t acc, int N, int8_t* dst, lon
   }
 }
 
+// The epilogue of an instance compiled for one moduli count kN, called directly (measured
+// faster than the dispatch above); kN = 0: any N, through the dispatch.
+template <int kN>
+__device__ __noinline__ void prep_epilogue_fixed(uint32_t acc, int8_t* dst, long long pb,
+                                                 bool store) {
+  tc_fence_after();  // the TMEM reads follow the completion seen on the mbarrier
+  const uint32_t taddr = acc + ((uint32_t)(((threadIdx.x >> 5) & 3) * 32) << 16);
+  prep_epilogue_n<kN>(taddr, dst, pb, store);
+}
+template <int kN>
+__device__ __forceinline__ void prep_epilogue_of(uint32_t acc, int N, int8_t* dst, long long pb,
+                                                 bool store) {
+  if constexpr (kN > 0) prep_epilogue_fixed<kN>(acc, dst, pb, store);
+  else prep_epilogue(acc, N, dst, pb, store);
+}
+
 // Image byte offset of (row r, K position q) inside a plane (ggemm_stages.h).
 __device__ __forceinline__ long long img_off(int rg, int r, int q) {
   const int rr = r & 7, qq = q & 31;
@@ -382,7 +398,7 @@ __device__ __forceinline__ long long img_off(int rg, int r, int q) {
 // half w / 4 (chains 4 (w / 4) .. +3) owns the 4 quads of its parity; MMA row 32 j + r of the
 // half's tile holds quad (w / 4) + 2 j of row r, and the epilogue thread (warp w, lane r)
 // owns quad (w / 4) + 2 (w % 4).
-template <bool kBias>
+template <bool kBias, int kN>
 __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters* cnt,
                                 PrepSmem& sm, uint32_t tmem, int n_cols) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -485,7 +501,7 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
     int8_t* prev_dst = d.img + img_off(rg, r, k0 - 32 + 4 * qe);
     if (!prep_round<kBias>(sm, tmem, n_cols, i, i > 0,
                     [&](uint32_t col) {
-                      prep_epilogue(tmem + col, N, prev_dst, d.plane_bytes, in_image);
+                      prep_epilogue_of<kN>(tmem + col, N, prev_dst, d.plane_bytes, in_image);
                     },
                     cnt))
       break;
@@ -497,7 +513,7 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
   }
   if (i == ksteps && ksteps > 0 &&
       prep_wait(sm, half, (i - 1) & 1, (uint32_t)((i - 1) >> 1) & 1u, cnt))
-    prep_epilogue(tmem + prep_region<kBias>(n_cols, half, kBias ? 0 : (i - 1) & 1), N,
+    prep_epilogue_of<kN>(tmem + prep_region<kBias>(n_cols, half, kBias ? 0 : (i - 1) & 1), N,
                   d.img + img_off(rg, r, 32 * (i - 1) + 4 * qe), d.plane_bytes, in_image);
   __syncthreads();
   sm.a[w][lane] = da;
@@ -521,7 +537,7 @@ __device__ void prep_rows_block(const ggemm_prep_desc_t& d, int blk, DevCounters
 // xor butterfly.  In a round (128 K positions) lane L of warp w takes positions c0 + 4 L + e,
 // e = 0..3, of its column: its own MMA row (32 (w % 4) + L of tile w / 4), so the same thread
 // writes the slots and reads back the residues.
-template <bool kBias>
+template <bool kBias, int kN>
 __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters* cnt,
                                 PrepSmem& sm, uint32_t tmem, int n_cols) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -603,7 +619,7 @@ __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters
     const bool in_kp = qp >= 0 && (qp >> 5) < ksteps;
     int8_t* prev_dst = d.img + img_off(rg, col, in_kp ? qp : 0);
     if (!prep_round<kBias>(sm, tmem, n_cols, i, i > 0,
-                    [&](uint32_t c) { prep_epilogue(tmem + c, N, prev_dst, d.plane_bytes, in_kp); },
+                    [&](uint32_t c) { prep_epilogue_of<kN>(tmem + c, N, prev_dst, d.plane_bytes, in_kp); },
                     cnt))
       break;
 #pragma unroll
@@ -616,7 +632,7 @@ __device__ void prep_cols_block(const ggemm_prep_desc_t& d, int blk, DevCounters
       prep_wait(sm, w >> 2, (i - 1) & 1, (uint32_t)((i - 1) >> 1) & 1u, cnt)) {
     const int qp = 128 * (i - 1) + 4 * lane;
     const bool in_kp = (qp >> 5) < ksteps;
-    prep_epilogue(tmem + prep_region<kBias>(n_cols, w >> 2, kBias ? 0 : (i - 1) & 1), N,
+    prep_epilogue_of<kN>(tmem + prep_region<kBias>(n_cols, w >> 2, kBias ? 0 : (i - 1) & 1), N,
                   d.img + img_off(rg, col, in_kp ? qp : 0), d.plane_bytes, in_kp);
   }
 #pragma unroll
@@ -660,10 +676,11 @@ __device__ __forceinline__ int find_owner_warp(const P* __restrict__ prefix, int
   return lo;
 }
 
-// Compiled twice: kBias = false for descriptors with N <= 15, true for N > 15 (the host
-// launches each on its own range of the descriptor array; prefix values are absolute and the
-// grid's blocks start at block block0 of that numbering).
-template <bool kBias>
+// Compiled per class of moduli counts (prep_class): kN = 14, 15, 16 for that count only, kN = 0
+// for the other counts with kBias = prep_needs_bias(N).  The host launches each on its own range
+// of the descriptor array; prefix values are absolute and the grid's blocks start at block
+// block0 of that numbering.
+template <bool kBias, int kN>
 __global__ void __launch_bounds__(kPrepThreads, 2)
     prep_kernel(const ggemm_prep_desc_t* __restrict__ descs, const int* __restrict__ prefix,
                 int num, int block0, DevCounters* cnt) {
@@ -672,7 +689,9 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
   const int bl = block0 + (int)blockIdx.x;
   const int owner = find_owner_warp(prefix, num, bl);
   const ggemm_prep_desc_t d = descs[owner];
-  if (d.N < 1 || d.N > kMaxModuli || d.rows <= 0 || prep_needs_bias(d.N) != kBias) return;
+  if (d.N < 1 || d.N > kMaxModuli || d.rows <= 0 || prep_needs_bias(d.N) != kBias ||
+      (kN > 0 && d.N != kN))
+    return;
   const int n_cols = (4 * (d.N + 1) + 15) / 16 * 16;
   load_weights(sm, d.N, n_cols, (d.kind & GGEMM_PREP_QSCALED) != 0);
   if (threadIdx.x == 0) {
@@ -701,8 +720,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     tmem_st_wait();
   }
   const int blk = bl - prefix[owner];
-  if ((d.kind & 1) == 0) prep_rows_block<kBias>(d, blk, cnt, sm, tmem, n_cols);
-  else prep_cols_block<kBias>(d, blk, cnt, sm, tmem, n_cols);
+  if ((d.kind & 1) == 0) prep_rows_block<kBias, kN>(d, blk, cnt, sm, tmem, n_cols);
+  else prep_cols_block<kBias, kN>(d, blk, cnt, sm, tmem, n_cols);
   // a half that gave up may still have MMAs in flight (at most its last two rounds, since
   // every round waits for the one before): let them finish (bounded) first
   __syncthreads();
@@ -1638,9 +1657,15 @@ int upload_tables_current_device() {
   if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kGemmSmem) != cudaSuccess)
     return 3;
-  if (cudaFuncSetAttribute(prep_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(prep_kernel<false, 14>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kPrepSmem) != cudaSuccess ||
-      cudaFuncSetAttribute(prep_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaFuncSetAttribute(prep_kernel<false, 15>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kPrepSmem) != cudaSuccess ||
+      cudaFuncSetAttribute(prep_kernel<false, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kPrepSmem) != cudaSuccess ||
+      cudaFuncSetAttribute(prep_kernel<true, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kPrepSmem) != cudaSuccess ||
+      cudaFuncSetAttribute(prep_kernel<true, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kPrepSmem) != cudaSuccess)
     return 3;
   g_gemm_attr[dev] = true;
@@ -1657,18 +1682,24 @@ int current_device_sms() {
   return g_sms[dev] > 0 ? g_sms[dev] : 148;
 }
 
-int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, int num, int num_lo,
-                int blocks_lo, int total_blocks, DevCounters* cnt, cudaStream_t s,
-                int* launches) {
+int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, const PrepSplit& sp,
+                DevCounters* cnt, cudaStream_t s, int* launches) {
   int n = 0;
-  if (num_lo > 0 && blocks_lo > 0) {
-    prep_kernel<false><<<blocks_lo, kPrepThreads, kPrepSmem, s>>>(d_descs, d_prefix, num_lo, 0,
-                                                                   cnt);
-    ++n;
-  }
-  if (num > num_lo && total_blocks > blocks_lo) {
-    prep_kernel<true><<<total_blocks - blocks_lo, kPrepThreads, kPrepSmem, s>>>(
-        d_descs + num_lo, d_prefix + num_lo, num - num_lo, blocks_lo, cnt);
+  for (int c = 0; c < kPrepClasses; ++c) {
+    const int f = sp.first[c], num = sp.first[c + 1] - f;
+    const long long blocks = sp.block0[c + 1] - sp.block0[c];
+    if (num <= 0 || blocks <= 0) continue;
+    const ggemm_prep_desc_t* dd = d_descs + f;
+    const int* pp = d_prefix + f;
+    const int b0 = (int)sp.block0[c];
+    const unsigned g = (unsigned)blocks;
+    switch (c) {
+      case 0: prep_kernel<false, 14><<<g, kPrepThreads, kPrepSmem, s>>>(dd, pp, num, b0, cnt); break;
+      case 1: prep_kernel<false, 15><<<g, kPrepThreads, kPrepSmem, s>>>(dd, pp, num, b0, cnt); break;
+      case 2: prep_kernel<false, 0><<<g, kPrepThreads, kPrepSmem, s>>>(dd, pp, num, b0, cnt); break;
+      case 3: prep_kernel<true, 16><<<g, kPrepThreads, kPrepSmem, s>>>(dd, pp, num, b0, cnt); break;
+      default: prep_kernel<true, 0><<<g, kPrepThreads, kPrepSmem, s>>>(dd, pp, num, b0, cnt); break;
+    }
     ++n;
   }
   if (launches) *launches += n;

@@ -4,6 +4,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "ggemm_stages.h"
 
 namespace g2 {
@@ -96,13 +98,41 @@ int current_device_sms();
 
 // Launchers: one kernel each on `s`.  prefix: device array of num+1 exclusive block / tile
 // prefix sums.  Return cudaError_t of the launch.
-// Prep: descriptors [0, num_lo) have N <= 15 (prep_needs_bias false) and own blocks
-// [0, blocks_lo) of the prefix numbering; the rest have N > 15.  One launch per non-empty range
-// (the kernel is compiled once per case); *launches, when given, is increased by their number.
+// Prep is compiled per class of moduli counts: N = 14, 15 and 16 (the counts the N selection
+// gives for k up to 2^16) each get an instance with their epilogue called directly; the other
+// counts share one instance per accumulator mode (N <= 15 / N > 15) that dispatches on N.
 __host__ __device__ constexpr inline bool prep_needs_bias(int N) { return N > 15; }
-int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, int num, int num_lo,
-                int blocks_lo, int total_blocks, DevCounters* cnt, cudaStream_t s,
-                int* launches = nullptr);
+constexpr int kPrepClasses = 5;
+inline int prep_class(int N) { return N == 14 ? 0 : N == 15 ? 1 : N <= 15 ? 2 : N == 16 ? 3 : 4; }
+// Descriptors sorted by class: class c owns descriptors [first[c], first[c + 1]) and blocks
+// [block0[c], block0[c + 1]) of the prefix numbering.
+struct PrepSplit {
+  int first[kPrepClasses + 1];
+  long long block0[kPrepClasses + 1];
+};
+// Sorts descs[0, num) by class (stable; descriptors are independent), writes the exclusive
+// block prefix (num + 1 entries) and the split.
+inline void prep_partition(ggemm_prep_desc_t* descs, int num, int* prefix, PrepSplit* sp) {
+  std::stable_sort(descs, descs + num, [](const ggemm_prep_desc_t& a, const ggemm_prep_desc_t& b) {
+    return prep_class(a.N) < prep_class(b.N);
+  });
+  long long blocks = 0;
+  int x = 0;
+  for (int c = 0; c < kPrepClasses; ++c) {
+    sp->first[c] = x;
+    sp->block0[c] = blocks;
+    for (; x < num && prep_class(descs[x].N) == c; ++x) {
+      prefix[x] = (int)blocks;
+      blocks += prep_blocks(descs[x]);
+    }
+  }
+  sp->first[kPrepClasses] = num;
+  sp->block0[kPrepClasses] = blocks;
+  prefix[num] = (int)blocks;
+}
+// One launch per non-empty class; *launches, when given, is increased by their number.
+int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, const PrepSplit& sp,
+                DevCounters* cnt, cudaStream_t s, int* launches = nullptr);
 int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long long total_tiles,
                 DevCounters* cnt, cudaStream_t s);
 // Blocks per job: recon_job_blocks.

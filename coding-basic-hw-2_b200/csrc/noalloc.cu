@@ -202,11 +202,16 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
   DevCounters* cnt = reinterpret_cast<DevCounters*>(base + kOffCounters);
   noalloc_setup_kernel<<<1, 32, 0, stream>>>(d);
   if (cudaGetLastError() != cudaSuccess) return GGEMM_ERR_CUDA;
+  PrepSplit sp;  // both descriptors have N moduli: one prep instance
+  for (int c = 0; c <= kPrepClasses; ++c) {
+    const bool after = c > prep_class(N);
+    sp.first[c] = after ? nprep : 0;
+    sp.block0[c] = after ? prep_blocks_total : 0;
+  }
   if (nprep &&
       launch_prep(reinterpret_cast<const ggemm_prep_desc_t*>(db + offsetof(NoAllocDescs, prep)),
-                  reinterpret_cast<const int*>(db + offsetof(NoAllocDescs, prep_prefix)), nprep,
-                  prep_needs_bias(N) ? 0 : nprep, prep_needs_bias(N) ? 0 : prep_blocks_total,
-                  prep_blocks_total, cnt, stream))
+                  reinterpret_cast<const int*>(db + offsetof(NoAllocDescs, prep_prefix)), sp, cnt,
+                  stream))
     return GGEMM_ERR_NUMERICS;
   if (d.job_prefix[1] > 0 &&
       launch_gemm(reinterpret_cast<const GemmJob*>(db + offsetof(NoAllocDescs, job)),

@@ -45,7 +45,7 @@ extern "C" int ggemm_stage_prep(const ggemm_prep_desc_t* descs, int num, void* s
   size_t off_p;
   const size_t bytes = blob_layout(num, sizeof(ggemm_prep_desc_t), sizeof(int), &off_p);
   t_stage.assign(bytes, 0);
-  // descriptors are independent: those with N <= 15 go first (launch_prep)
+  // descriptors are independent: sorted by prep instance (launch_prep)
   ggemm_prep_desc_t* sd = reinterpret_cast<ggemm_prep_desc_t*>(t_stage.data());
   std::memcpy(sd, descs, (size_t)num * sizeof(ggemm_prep_desc_t));
   for (int i = 0; i < num; ++i) {
@@ -57,24 +57,20 @@ extern "C" int ggemm_stage_prep(const ggemm_prep_desc_t* descs, int num, void* s
         (size_t)d.plane_bytes < ggemm_img_plane_bytes(d.rows, d.k))
       return GGEMM_ERR_INVALID;
   }
-  std::stable_partition(sd, sd + num,
-                        [](const ggemm_prep_desc_t& d) { return !prep_needs_bias(d.N); });
-  int* pre = reinterpret_cast<int*>(t_stage.data() + off_p);
-  long long blocks = 0, blocks_lo = 0;
-  int num_lo = 0;
+  long long blocks = 0;
   for (int i = 0; i < num; ++i) {
-    pre[i] = (int)blocks;
     blocks += prep_blocks(sd[i]);
     if (blocks > 0x7FFFFFFF) return GGEMM_ERR_INVALID;
-    if (!prep_needs_bias(sd[i].N)) ++num_lo, blocks_lo = blocks;
   }
-  pre[num] = (int)blocks;
+  int* pre = reinterpret_cast<int*>(t_stage.data() + off_p);
+  PrepSplit sp;
+  prep_partition(sd, num, pre, &sp);
   int r = copy_blob(scratch, scratch_bytes, bytes, s);
   if (r) return r;
   const char* db = static_cast<const char*>(scratch);
   return launch_prep(reinterpret_cast<const ggemm_prep_desc_t*>(db),
-                     reinterpret_cast<const int*>(db + off_p), num, num_lo, (int)blocks_lo,
-                     (int)blocks, static_cast<DevCounters*>(counters), s)
+                     reinterpret_cast<const int*>(db + off_p), sp,
+                     static_cast<DevCounters*>(counters), s)
              ? GGEMM_ERR_NUMERICS
              : GGEMM_OK;
 }
