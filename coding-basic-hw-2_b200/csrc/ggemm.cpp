@@ -423,7 +423,6 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
     }
     if (!loop) jp[jq] = tiles;
     ch.tiles = tiles;
-    long long rb = 0;
     for (int x = 0; x < ch.count; ++x) {
       const int j = ch.first + x;
       const int g = emu[j];
@@ -448,11 +447,10 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       d.c_plane = y8 ? (long long)y8_plane_bytes(p.m, p.n) : (long long)c_plane_elems(p.m, p.n);
       d.rs = h->wsA + h->ua_ws[h->ua_of[j]];
       d.cs = h->wsB + h->ub_ws[h->ub_of[j]];
-      rp[x] = rb;
-      rb += recon_job_blocks(d);
     }
-    rp[ch.count] = rb;
-    ch.recon_blocks = rb;
+    // descriptors sorted by reconstruct instance (launch_recon)
+    recon_partition(rd, ch.count, rp, &ch.recon_split);
+    ch.recon_blocks = ch.recon_split.block0[kReconClasses];
     c.nprep_total += np;
   }
 
@@ -542,10 +540,9 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
     if (!mark(2)) return GGEMM_ERR_CUDA;
     if (ch.recon_blocks > 0) {
       if (launch_recon(reinterpret_cast<const ggemm_recon_desc_t*>(db + ch.off_recon),
-                       reinterpret_cast<const long long*>(db + ch.off_recon_prefix), ch.count,
-                       ch.recon_blocks, repair, h->counters, s))
+                       reinterpret_cast<const long long*>(db + ch.off_recon_prefix),
+                       ch.recon_split, repair, h->counters, s, launches))
         return GGEMM_ERR_NUMERICS;
-      ++*launches;
     }
     if (!mark(3)) return GGEMM_ERR_CUDA;
   }

@@ -46,7 +46,8 @@ struct Chunk {
   int first, count;        // range in emu order
   size_t off_prep, off_prep_prefix, off_jobs, off_job_prefix, off_recon, off_recon_prefix;
   int num_prep, prep_blocks;
-  PrepSplit prep_split;  // descriptors sorted by prep instance (launch_prep)
+  PrepSplit prep_split;    // descriptors sorted by prep instance (launch_prep)
+  ReconSplit recon_split;  // ... by reconstruct instance (launch_recon)
   bool qscale;  // A images q-scaled (every problem of the chunk in the digit layout)
   long long tiles, recon_blocks;
 };

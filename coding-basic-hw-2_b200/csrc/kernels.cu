@@ -1475,6 +1475,7 @@ __device__ __noinline__ void recon_c32_block(const ggemm_recon_desc_t* __restric
 // first arithmetic.  The CRT sums run plane by plane over the thread's 8 entries, so each
 // plane's weights are read once per thread instead of once per entry.  Column statistics are
 // staged in shared memory.  Every thread of the block calls it.
+template <int kN>
 __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long long local,
                                                int mode, unsigned& n_unc, unsigned& n_rep,
                                                unsigned& n_saf) {
@@ -1496,7 +1497,8 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
   }
   __syncthreads();
   if (!ok_desc || i >= d.m) return;
-  const ReconCtx cx = recon_ctx(d);
+  ReconCtx cx = recon_ctx(d);
+  if constexpr (kN > 0) cx.N = kN;  // an instance for this moduli count only (host-sorted)
   const int N = cx.N;
   const int j0 = ch * 16 + cg * 8;
   const int ncol = min(8, d.n - j0);
@@ -1587,18 +1589,25 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
   }
 }
 
-// One launch over every problem of a call; the layout is chosen per problem (block-uniform).
-// Compiled once per repair mode (GGEMM_STAGE_REPAIR_*), so the digit-layout body carries only
-// its mode's certificate / repair branches.
-template <int kMode>
+// One launch per class of moduli counts over its problems (recon_class; prefix values are
+// absolute, the grid starts at block block0); the layout is chosen per problem (block-uniform).
+// Compiled per repair mode (GGEMM_STAGE_REPAIR_*), so the digit-layout body carries only its
+// mode's certificate / repair branches, and per moduli count kN = 14, 15, 16 (kN = 0: any N), so
+// that its CRT loops and constant-table offsets are resolved at compile time.
+template <int kMode, int kN>
 __global__ void __launch_bounds__(kReconThreads, 2)
     recon_kernel(const ggemm_recon_desc_t* __restrict__ descs,
-                 const long long* __restrict__ prefix, int num, DevCounters* cnt) {
-  const int owner = find_owner_warp(prefix, num, (long long)blockIdx.x);
+                 const long long* __restrict__ prefix, int num, long long block0,
+                 DevCounters* cnt) {
+  const long long bl = block0 + (long long)blockIdx.x;
+  const int owner = find_owner_warp(prefix, num, bl);
   const ggemm_recon_desc_t d = descs[owner];
-  const long long local = (long long)blockIdx.x - prefix[owner];
+  const long long local = bl - prefix[owner];
   unsigned n_unc = 0, n_rep = 0, n_saf = 0;
-  if (d.layout == GGEMM_PRODUCTS_DIGITS) recon_y8_block(d, local, kMode, n_unc, n_rep, n_saf);
+  if (d.layout == GGEMM_PRODUCTS_DIGITS) {
+    if (kN > 0 && d.N != kN) return;  // not this instance's (the host never launches it so)
+    recon_y8_block<kN>(d, local, kMode, n_unc, n_rep, n_saf);
+  }
   else recon_c32_block(descs + owner, local, kMode, n_unc, n_rep, n_saf);
   flush_counters(n_unc, n_rep, n_saf, cnt);
 }
@@ -1715,25 +1724,39 @@ int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long 
   return (int)cudaGetLastError();
 }
 
-int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix, int num,
-                 long long total_blocks, int mode, DevCounters* cnt, cudaStream_t s) {
-  if (num <= 0 || total_blocks <= 0) return 0;
-  if (total_blocks > 0x7FFFFFFFLL) return (int)cudaErrorInvalidConfiguration;
-  const unsigned grid = (unsigned)total_blocks;
-  switch (mode) {
-    case GGEMM_STAGE_REPAIR_OFF:
-      recon_kernel<GGEMM_STAGE_REPAIR_OFF><<<grid, kReconThreads, 0, s>>>(d_descs, d_prefix, num,
-                                                                          cnt);
-      break;
-    case GGEMM_STAGE_REPAIR_COUNT:
-      recon_kernel<GGEMM_STAGE_REPAIR_COUNT><<<grid, kReconThreads, 0, s>>>(d_descs, d_prefix,
-                                                                            num, cnt);
-      break;
-    default:
-      recon_kernel<GGEMM_STAGE_REPAIR_ON><<<grid, kReconThreads, 0, s>>>(d_descs, d_prefix, num,
-                                                                         cnt);
-      break;
+template <int kMode>
+static void launch_recon_mode(int c, const ggemm_recon_desc_t* dd, const long long* pp, int num,
+                              unsigned grid, long long b0, DevCounters* cnt, cudaStream_t s) {
+  switch (c) {
+    case 0: recon_kernel<kMode, 14><<<grid, kReconThreads, 0, s>>>(dd, pp, num, b0, cnt); break;
+    case 1: recon_kernel<kMode, 15><<<grid, kReconThreads, 0, s>>>(dd, pp, num, b0, cnt); break;
+    case 2: recon_kernel<kMode, 16><<<grid, kReconThreads, 0, s>>>(dd, pp, num, b0, cnt); break;
+    default: recon_kernel<kMode, 0><<<grid, kReconThreads, 0, s>>>(dd, pp, num, b0, cnt); break;
   }
+}
+
+int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix,
+                 const ReconSplit& sp, int mode, DevCounters* cnt, cudaStream_t s,
+                 int* launches) {
+  int n = 0;
+  for (int c = 0; c < kReconClasses; ++c) {
+    const int f = sp.first[c], num = sp.first[c + 1] - f;
+    const long long blocks = sp.block0[c + 1] - sp.block0[c];
+    if (num <= 0 || blocks <= 0) continue;
+    if (blocks > 0x7FFFFFFFLL) return (int)cudaErrorInvalidConfiguration;
+    const unsigned grid = (unsigned)blocks;
+    if (mode == GGEMM_STAGE_REPAIR_OFF)
+      launch_recon_mode<GGEMM_STAGE_REPAIR_OFF>(c, d_descs + f, d_prefix + f, num, grid,
+                                                sp.block0[c], cnt, s);
+    else if (mode == GGEMM_STAGE_REPAIR_COUNT)
+      launch_recon_mode<GGEMM_STAGE_REPAIR_COUNT>(c, d_descs + f, d_prefix + f, num, grid,
+                                                  sp.block0[c], cnt, s);
+    else
+      launch_recon_mode<GGEMM_STAGE_REPAIR_ON>(c, d_descs + f, d_prefix + f, num, grid,
+                                               sp.block0[c], cnt, s);
+    ++n;
+  }
+  if (launches) *launches += n;
   return (int)cudaGetLastError();
 }
 

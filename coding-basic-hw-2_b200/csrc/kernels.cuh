@@ -135,8 +135,40 @@ int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, const Pre
                 DevCounters* cnt, cudaStream_t s, int* launches = nullptr);
 int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long long total_tiles,
                 DevCounters* cnt, cudaStream_t s);
-// Blocks per job: recon_job_blocks.
-int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix, int num,
-                 long long total_blocks, int mode, DevCounters* cnt, cudaStream_t s);
+// Reconstruct: compiled per repair mode and per class of moduli counts (N = 14, 15, 16 each, the
+// rest together); descriptors sorted by class, class c owning descriptors [first[c],
+// first[c + 1]) and blocks [block0[c], block0[c + 1]) (blocks per descriptor: recon_job_blocks).
+constexpr int kReconClasses = 4;
+inline int recon_class(int N) { return N == 14 ? 0 : N == 15 ? 1 : N == 16 ? 2 : 3; }
+struct ReconSplit {
+  int first[kReconClasses + 1];
+  long long block0[kReconClasses + 1];
+};
+// Sorts descs[0, num) by class (stable; descriptors are independent), writes the exclusive
+// block prefix (num + 1 entries) and the split.
+inline void recon_partition(ggemm_recon_desc_t* descs, int num, long long* prefix,
+                            ReconSplit* sp) {
+  std::stable_sort(descs, descs + num,
+                   [](const ggemm_recon_desc_t& a, const ggemm_recon_desc_t& b) {
+                     return recon_class(a.N) < recon_class(b.N);
+                   });
+  long long blocks = 0;
+  int x = 0;
+  for (int c = 0; c < kReconClasses; ++c) {
+    sp->first[c] = x;
+    sp->block0[c] = blocks;
+    for (; x < num && recon_class(descs[x].N) == c; ++x) {
+      prefix[x] = blocks;
+      blocks += recon_job_blocks(descs[x]);
+    }
+  }
+  sp->first[kReconClasses] = num;
+  sp->block0[kReconClasses] = blocks;
+  prefix[num] = blocks;
+}
+// One launch per non-empty class; *launches, when given, is increased by their number.
+int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix,
+                 const ReconSplit& sp, int mode, DevCounters* cnt, cudaStream_t s,
+                 int* launches = nullptr);
 
 }  // namespace g2

@@ -218,9 +218,15 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
                   reinterpret_cast<const long long*>(db + offsetof(NoAllocDescs, job_prefix)), 1,
                   d.job_prefix[1], cnt, stream))
     return GGEMM_ERR_I8GEMM;
+  ReconSplit rsp;  // one descriptor: one reconstruct instance
+  for (int c = 0; c <= kReconClasses; ++c) {
+    const bool after = c > recon_class(N);
+    rsp.first[c] = after ? 1 : 0;
+    rsp.block0[c] = after ? d.recon_prefix[1] : 0;
+  }
   if (launch_recon(reinterpret_cast<const ggemm_recon_desc_t*>(db + offsetof(NoAllocDescs, recon)),
                    reinterpret_cast<const long long*>(db + offsetof(NoAllocDescs, recon_prefix)),
-                   1, d.recon_prefix[1], mode, cnt, stream))
+                   rsp, mode, cnt, stream))
     return GGEMM_ERR_NUMERICS;
   return GGEMM_OK;
 }

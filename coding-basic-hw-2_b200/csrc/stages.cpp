@@ -147,9 +147,10 @@ extern "C" int ggemm_stage_recon(const ggemm_recon_desc_t* descs, int num, int r
   size_t off_p;
   const size_t bytes = blob_layout(num, sizeof(ggemm_recon_desc_t), sizeof(long long), &off_p);
   t_stage.assign(bytes, 0);
-  std::memcpy(t_stage.data(), descs, (size_t)num * sizeof(ggemm_recon_desc_t));
+  // descriptors are independent: sorted by reconstruct instance (launch_recon)
+  ggemm_recon_desc_t* sd = reinterpret_cast<ggemm_recon_desc_t*>(t_stage.data());
+  std::memcpy(sd, descs, (size_t)num * sizeof(ggemm_recon_desc_t));
   long long* pre = reinterpret_cast<long long*>(t_stage.data() + off_p);
-  long long blocks = 0;
   for (int i = 0; i < num; ++i) {
     const ggemm_recon_desc_t& d = descs[i];
     if (d.m < 0 || d.n < 0 || d.k < 0 || d.N < 1 || d.N > kMaxModuli) return GGEMM_ERR_INVALID;
@@ -160,15 +161,14 @@ extern "C" int ggemm_stage_recon(const ggemm_recon_desc_t* descs, int num, int r
     } else if (d.layout != GGEMM_PRODUCTS_INT32) {
       return GGEMM_ERR_INVALID;
     }
-    pre[i] = blocks;
-    blocks += recon_job_blocks(d);
   }
-  pre[num] = blocks;
+  ReconSplit sp;
+  recon_partition(sd, num, pre, &sp);
   int r = copy_blob(scratch, scratch_bytes, bytes, s);
   if (r) return r;
   const char* db = static_cast<const char*>(scratch);
   return launch_recon(reinterpret_cast<const ggemm_recon_desc_t*>(db),
-                      reinterpret_cast<const long long*>(db + off_p), num, blocks, repair_mode,
+                      reinterpret_cast<const long long*>(db + off_p), sp, repair_mode,
                       static_cast<DevCounters*>(counters), s)
              ? GGEMM_ERR_NUMERICS
              : GGEMM_OK;

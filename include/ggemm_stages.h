@@ -129,8 +129,10 @@ size_t ggemm_stage_scratch_bytes(int num);
  * followed by a uint32 status word (0 = ok); 64 bytes, caller-allocated and zeroed. */
 #define GGEMM_STAGE_COUNTER_BYTES 64
 
-/* Each enqueues exactly one kernel on `s` (none when there is no work).  Descriptors are
- * HOST arrays; they are copied into `scratch` first.  Returns GGEMM_OK or GGEMM_ERR_*. */
+/* Each enqueues its kernel on `s` (none when there is no work): the GEMM one launch, prep and
+ * reconstruct one launch per class of moduli counts present (N = 14, 15, 16 and the others are
+ * compiled separately).  Descriptors are HOST arrays; they are copied into `scratch` first.
+ * Returns GGEMM_OK or GGEMM_ERR_*. */
 int ggemm_stage_prep(const ggemm_prep_desc_t* descs, int num, void* scratch,
                      size_t scratch_bytes, void* counters, cudaStream_t s);
 int ggemm_stage_gemm(const ggemm_gemm_desc_t* descs, int num, void* scratch,
