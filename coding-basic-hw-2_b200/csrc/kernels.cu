@@ -1479,8 +1479,6 @@ template <int kN>
 __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long long local,
                                                int mode, unsigned& n_unc, unsigned& n_rep,
                                                unsigned& n_saf) {
-  __shared__ int s_sh[2][16];      // csh, tau of the 16 columns
-  __shared__ double s_nrm[2][16];  // ||dB_j||, ||B'_j|| (float upper bounds, widened once)
   // block: kY8Rows rows x one 16-column digit record; thread: row i, columns j0 .. j0 + 7 (half
   // cg of the record).  A warp (16 rows) reads 256 contiguous bytes of a digit plane.
   const bool ok_desc = d.N >= 1 && d.N <= kMaxModuli && d.m > 0 && d.n > 0;
@@ -1489,13 +1487,6 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
   const int i = (int)(local - ch * rblocks) * kY8Rows + (threadIdx.x >> 1);
   const int cg = threadIdx.x & 1;
   const bool planes = ok_desc && d.alpha != 0.0 && d.k > 0;
-  if (threadIdx.x < 32) {
-    const int st = threadIdx.x >> 4, x = threadIdx.x & 15, j = ch * 16 + x;
-    const bool v = ok_desc && d.alpha != 0.0 && j < d.n;
-    s_sh[st][x] = v ? d.cs[st * d.n + j] : 0;
-    s_nrm[st][x] = v ? (double)__int_as_float(d.cs[(2 + st) * d.n + j]) : 0.0;
-  }
-  __syncthreads();
   if (!ok_desc || i >= d.m) return;
   ReconCtx cx = recon_ctx(d);
   if constexpr (kN > 0) cx.N = kN;  // an instance for this moduli count only (host-sorted)
@@ -1568,15 +1559,20 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
     for (int x = 0; x < 4; ++x) {
       if (xb + x >= ncol) break;
       double* cp = crow + (xb + x) * d.ldc;
-      const int cx8 = cg * 8 + xb + x;
-      const int csh = s_sh[0][cx8], tau = s_sh[1][cx8];
+      // the column's shifts and norms, read per entry (L1 hits: every row of the block reads
+      // the same 16 columns) instead of staged in shared memory behind a block barrier
+      const int jx = j0 + xb + x;
+      const bool av = d.alpha != 0.0;
+      const int csh = av ? __ldg(d.cs + jx) : 0, tau = av ? __ldg(d.cs + d.n + jx) : 0;
       if (const int sp = recon_special(d, cp, c0[x], rsh, csh, sig, tau)) {
         need_saf |= (sp == 2 ? 1u : 0u) << (xb + x);
         continue;
       }
       const int32_t L = x == 0 ? lq.x : x == 1 ? lq.y : x == 2 ? lq.z : lq.w;
       if (recon_finish(d, cx, mode, cp, c0[x], h ? S1[4 + x] : S1[x], h ? S2[4 + x] : S2[x], L,
-                       rsh, csh, sig, tau, da, na, s_nrm[0][cx8], s_nrm[1][cx8], n_unc))
+                       rsh, csh, sig, tau, da, na,
+                       (double)__int_as_float(__ldg(d.cs + 2 * d.n + jx)),
+                       (double)__int_as_float(__ldg(d.cs + 3 * d.n + jx)), n_unc))
         need_rep |= 1u << (xb + x);
     }
   }
