@@ -904,8 +904,8 @@ __device__ __forceinline__ void emit_record(const uint32_t (&v)[32], const Digit
     uint32_t w[8];
 #pragma unroll
     for (int g = 0; g < 8; ++g)
-      w[g] = digit_of<kQ>(v[4 * g], dc) | (digit_of<kQ>(v[4 * g + 1], dc) << 8) |
-             (digit_of<kQ>(v[4 * g + 2], dc) << 16) | (digit_of<kQ>(v[4 * g + 3], dc) << 24);
+      w[g] = pack4(digit_of<kQ>(v[4 * g], dc), digit_of<kQ>(v[4 * g + 1], dc),
+                   digit_of<kQ>(v[4 * g + 2], dc), digit_of<kQ>(v[4 * g + 3], dc));
     *reinterpret_cast<uint4*>(ydst) = make_uint4(w[0], w[1], w[2], w[3]);
     *reinterpret_cast<uint4*>(ydst + dstep) = make_uint4(w[4], w[5], w[6], w[7]);
   } else {
