@@ -96,8 +96,9 @@ int upload_tables_current_device();
 // Streaming multiprocessors of the current device (cached).
 int current_device_sms();
 
-// Launchers: one kernel each on `s`.  prefix: device array of num+1 exclusive block / tile
-// prefix sums.  Return cudaError_t of the launch.
+// Launchers, on `s`: the GEMM one kernel, prep and the reconstruct one kernel per class of
+// moduli counts present.  prefix: device array of num+1 exclusive block / tile prefix sums.
+// Return the cudaError_t of the launches.
 // Prep is compiled per class of moduli counts: N = 14, 15 and 16 (the counts the N selection
 // gives for k up to 2^16) each get an instance with their epilogue called directly; the other
 // counts share one instance per accumulator mode (N <= 15 / N > 15) that dispatches on N.
