@@ -1516,11 +1516,9 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
     na = (double)__int_as_float(__ldg(d.rs + 3 * d.m + i));
   }
   double* crow = d.C + i + (long long)j0 * d.ldc;
-  double c0[4];  // entries of C of the current half (the second half is prefetched to L2)
+  double c8[8];  // the thread's 8 entries of C
 #pragma unroll
-  for (int x = 0; x < 4; ++x) c0[x] = (d.beta != 0.0 && x < ncol) ? crow[x * d.ldc] : 0.0;
-  if (d.beta != 0.0)
-    for (int x = 4; x < ncol; ++x) prefetch_l2(crow + x * d.ldc);
+  for (int x = 0; x < 8; ++x) c8[x] = (d.beta != 0.0 && x < ncol) ? crow[x * d.ldc] : 0.0;
   // CRT sums of the 8 entries, plane by plane
   uint64_t S1[8];
   uint32_t S2[8];
@@ -1552,10 +1550,7 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
     const int xb = 4 * h;
     if (xb >= ncol) break;
     const int4 lq = h ? l1 : l0;
-    if (h)
-#pragma unroll
-      for (int x = 0; x < 4; ++x)
-        c0[x] = (d.beta != 0.0 && 4 + x < ncol) ? crow[(4 + x) * d.ldc] : 0.0;
+    const double* c0 = c8 + xb;
 #pragma unroll
     for (int x = 0; x < 4; ++x) {
       if (xb + x >= ncol) break;
