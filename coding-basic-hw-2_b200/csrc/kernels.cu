@@ -39,6 +39,17 @@ __device__ __forceinline__ double mul_pow2(double x, int e) {
   }
   return x;
 }
+// The same product without the branch: three clamped steps always (for |e| <= 1000 the second
+// and third multiply by 1.0), so a warp whose lanes straddle the bound does not diverge.
+__device__ __forceinline__ double mul_pow2_nb(double x, int e) {
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const int ee = max(-1000, min(1000, e));
+    x *= __longlong_as_double((long long)(ee + 1023) << 52);
+    e -= ee;
+  }
+  return x;
+}
 
 // max(m, |a|) on the bit patterns: non-negative doubles order like their unsigned bits, so
 // for finite and infinite |a| this is fmax(m, |a|).  A NaN element wins instead of being skipped;
@@ -1259,7 +1270,7 @@ __device__ __forceinline__ bool recon_finish(const ggemm_recon_desc_t& d, const 
   const long long X1 = (long long)S1 - (long long)Q * c_tab.P1[N];
   const double xr = (double)X1 + fma(-Q, c_tab.P2[N], s2d);
   const int esc = cx.lu1 - rsh - csh;
-  const double v = mul_pow2(xr, esc);
+  const double v = mul_pow2_nb(xr, esc);
   const double emu = (beta == 0.0) ? alpha * v : fma(alpha, v, beta * c0);
   if (mode == GGEMM_STAGE_REPAIR_OFF || (beta != 0.0 && !(fabs(c0) < INFINITY))) {
     *cp = emu;
@@ -1268,8 +1279,8 @@ __device__ __forceinline__ bool recon_finish(const ggemm_recon_desc_t& d, const 
   const double u = 0x1p-53;
   const double et = fma(da, nb, fma(na, db, da * db)) * (1.0 + 0x1p-40);
   const double Eu = fma(4.0 * u, fabs(xr), fma(et, cx.inv_u1, cx.crt_u)) * (1.0 + 0x1p-40);
-  const double E = mul_pow2(Eu, esc);
-  double lab = mul_pow2((double)L32, -(sig + tau));
+  const double E = mul_pow2_nb(Eu, esc);
+  double lab = mul_pow2_nb((double)L32, -(sig + tau));
   // fmax(lab, |v| - E): lab is never NaN, and a NaN difference keeps lab, as fmax does; the
   // sign of a zero result is erased below
   const double dv = fabs(v) - E;
