@@ -129,7 +129,10 @@ struct PrepSmem {
   uint64_t bar[2][2];    // [half][buffer]: MMAs of a round complete
   uint64_t ready[2][2];  // [half][buffer]: the half's 4 warps wrote the round's slots
   uint32_t tmem;
-  int abort;
+  // per half: gave up after a timed-out wait.  Only the half's own threads write it, before
+  // they arrive at the half's next barrier, so every thread of the half reads the same value
+  // after that barrier and the half leaves its rounds together.
+  int abort[2];
   int issued[2], waited[2];  // per half: rounds whose MMAs were issued / seen complete
 };
 constexpr size_t kPrepSmem = 1024 + sizeof(PrepSmem);
@@ -238,11 +241,11 @@ __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, ui
 __device__ __forceinline__ bool prep_wait(PrepSmem& sm, int half, int bf, uint32_t parity,
                                           DevCounters* cnt) {
   if (mbar_try_wait(&sm.bar[half][bf], parity) ||
-      mbar_wait(&sm.bar[half][bf], parity, global_timer_ns() + 4000000000ull, &sm.abort)) {
+      mbar_wait(&sm.bar[half][bf], parity, global_timer_ns() + 4000000000ull, &sm.abort[half])) {
     if ((threadIdx.x & 127) == 0) ++sm.waited[half];
     return true;
   }
-  sm.abort = 1;
+  sm.abort[half] = 1;
   atomicCAS(&cnt->status, 0u, (unsigned)kStatusPrepTimeout);
   return false;
 }
@@ -257,9 +260,9 @@ __device__ __forceinline__ void half_sync(int half) {
 __device__ __forceinline__ bool prep_wait_ready(PrepSmem& sm, int half, int i, DevCounters* cnt) {
   uint64_t* b = &sm.ready[half][i & 1];
   const uint32_t parity = (uint32_t)(i >> 1) & 1u;
-  if (mbar_try_wait(b, parity) || mbar_wait(b, parity, global_timer_ns() + 4000000000ull, &sm.abort))
+  if (mbar_try_wait(b, parity) || mbar_wait(b, parity, global_timer_ns() + 4000000000ull, &sm.abort[half]))
     return true;
-  sm.abort = 1;
+  sm.abort[half] = 1;
   atomicCAS(&cnt->status, 0u, (unsigned)kStatusPrepTimeout);
   return false;
 }
@@ -311,12 +314,12 @@ __device__ __forceinline__ bool prep_round(PrepSmem& sm, uint32_t tmem, int n_co
       tc_fence_after();
       prep_issue<kBias>(sm, tmem, n_cols, half, i);
     }
-    __syncwarp();
-    if (sm.abort) return false;
+    // warp-uniform: the next round's __syncwarp needs every lane
+    if (__any_sync(0xFFFFFFFFu, *(volatile int*)&sm.abort[half] != 0)) return false;
   } else {
     half_sync(half);
     tc_fence_after();
-    if (sm.abort) return false;
+    if (sm.abort[half]) return false;
     if ((threadIdx.x & 127) == 0) prep_issue<kBias>(sm, tmem, n_cols, half, i);
   }
   if (dbuf && prev && prep_wait(sm, half, pb, pp, cnt)) epi(prep_region<kBias>(n_cols, half, pb));
@@ -714,7 +717,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
       sm.issued[h] = 0;
       sm.waited[h] = 0;
     }
-    sm.abort = 0;
+    sm.abort[0] = 0;
+    sm.abort[1] = 0;
     fence_mbar_init();
   }
   if (threadIdx.x < 32) {
