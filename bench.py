@@ -48,6 +48,11 @@ def c2_shapes(num: int, seed: int = SEED):
     return [(int(m[i]), int(n[i]), int(k[i]), float(alpha[i]), 0.5) for i in range(num)]
 
 
+def c3_shapes(num: int):
+    """Config C3 of the survey: num problems of 8192^3, alpha = 1, beta = 0 (INT8-bound)."""
+    return [(8192, 8192, 8192, 1.0, 0.0)] * num
+
+
 def fill_phi(t, phi: float, seed: int):
     """(U - 0.5) * exp(phi * N(0,1)) in place (device generator, deterministic per seed)."""
     import torch
@@ -65,7 +70,7 @@ def fill_phi(t, phi: float, seed: int):
 class Group:
     """Device buffers of one rank's problems (tight leading dimensions)."""
 
-    def __init__(self, g2, shapes, seeds, device):
+    def __init__(self, g2, shapes, seeds, device, phi=PHI):
         import torch
 
         self.shapes = shapes
@@ -80,8 +85,8 @@ class Group:
         oa = ob = oc = 0
         entries = []
         for (m, n, k, alpha, beta), sd in zip(shapes, seeds):
-            fill_phi(self.A[oa:oa + m * k], PHI, sd * 4 + 1)
-            fill_phi(self.B[ob:ob + k * n], PHI, sd * 4 + 2)
+            fill_phi(self.A[oa:oa + m * k], phi, sd * 4 + 1)
+            fill_phi(self.B[ob:ob + k * n], phi, sd * 4 + 2)
             fill_phi(self.C0[oc:oc + m * n], 0.0, sd * 4 + 3)
             self.C0[oc:oc + m * n].mul_(2.0)  # U[-1, 1)
             entries.append(dict(m=m, n=n, k=k, A=self.A.data_ptr() + 8 * oa, lda=m,
@@ -329,7 +334,8 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
 
     # global group, then this rank's shard
-    gshapes = c2_shapes(args.problems * world)
+    c3 = args.workload == "c3"
+    gshapes = c3_shapes(args.problems * world) if c3 else c2_shapes(args.problems * world)
     if world > 1:
         logical = g2.make_problems([dict(m=m, n=n, k=k, A=0x1000 * (i + 1), lda=m,
                                          B=0x100000000 * (i + 1), ldb=k,
@@ -348,11 +354,11 @@ def run_ours(args):
         seeds = [SEED + 1000 * i for i in range(len(shapes))]
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.set_stream(stream)
-    grp = Group(g2, shapes, seeds, dev)
+    grp = Group(g2, shapes, seeds, dev, phi=0.5 if c3 else PHI)
     torch.cuda.synchronize()
     sptr = stream.cuda_stream
     handle = g2.Handle(max(1, grp.num), grp.na, grp.nb, grp.nc, stream=sptr)
-    cfg = g2.config(num_moduli=0, target_rel_err=1e-15, allow_fallback=1)
+    cfg = g2.config(num_moduli=16 if c3 else 0, target_rel_err=1e-15, allow_fallback=1)
 
     def call(path=g2.PATH_EMU_GROUPED):
         rc, st = handle.grouped_dgemm(path, cfg, grp.problems, grp.num)
@@ -415,11 +421,27 @@ def run_ours(args):
     value = flops_all * args.steps / t_max / 1e12
 
     if args.quick:
+        line = {"quick": True, "workload": args.workload, "value": value, "unit": "TFLOP/s",
+                "ms_per_step": t_max / args.steps * 1e3,
+                "stage_ms": [float(x) for x in stage_ms], "problems_per_gpu": grp.num,
+                "moduli": nmod}
+        if c3:  # cuBLAS DGEMM on the same data, and the GEMM stage's INT8 rate
+            for _ in range(2):
+                call(g2.PATH_NATIVE_GROUPED)
+            barrier()
+            n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n0.record(stream)
+            for _ in range(args.steps):
+                call(g2.PATH_NATIVE_GROUPED)
+            n1.record(stream)
+            barrier()
+            line["cublas_dgemm_tflops"] = flops_all * args.steps / max_over_ranks(
+                n0.elapsed_time(n1) / 1e3) / 1e12
+            ops = sum(2.0 * m * n * ((k + 31) // 32 * 32) * (nmod + 1)
+                      for m, n, k, _, _ in grp.shapes)
+            line["gemm_int8_tops"] = ops / (stage_ms[1] / 1e3) / 1e12
         if rank == 0:
-            print(json.dumps({"quick": True, "value": value, "unit": "TFLOP/s",
-                              "ms_per_step": t_max / args.steps * 1e3,
-                              "stage_ms": [float(x) for x in stage_ms],
-                              "problems_per_gpu": grp.num, "moduli": nmod}), flush=True)
+            print(json.dumps(line), flush=True)
         handle.close()
         if world > 1:
             dist.barrier()
@@ -591,12 +613,21 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--problems", type=int, default=PROBS_PER_GPU,
                     help="problems per GPU (64 = the C2 workload; fewer for profiling)")
+    ap.add_argument("--workload", choices=["c2", "c3"], default="c2",
+                    help="c2: the bench line's workload; c3: 8192^3 problems, N = 16, "
+                         "--quick only (device timing, cuBLAS DGEMM beside it)")
     ap.add_argument("--quick", action="store_true",
                     help="device-resident timing only (profiling runs): no e2e, cuBLAS, "
                          "certified or CPU legs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "c3":
+        if args.impl == "reference":
+            ap.error("--workload c3 times this library only")
+        args.quick = True
+        if args.problems == PROBS_PER_GPU:
+            args.problems = 8
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_ours(args)
