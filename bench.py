@@ -2,21 +2,22 @@
 """bench.py -- effective FP64 TFLOP/s of the emulated grouped DGEMM on B200.
 
 Metric: effective FP64 TFLOP/s = sum_g 2 m_g n_g k_g / t for one
-ggemm_grouped_dgemm call over the whole group (EMU_GROUPED path, adaptive moduli), next to
-cuBLAS native DGEMM on the same data, plus the certified fraction of outputs.
+ggemm_grouped_dgemm call over the whole group, next to cuBLAS native DGEMM on the same data, the
+reference library (its own sources built for sm_100a, oracle/_ref) on the same device buffers,
+the INT8-roofline-implied bound and the certified fraction of outputs.
 
-Default workload (configs[1] of BASELINE.json, "C2"): G = 64 problems, m, n, k drawn uniformly
-from {128, 192, ..., 2048}; entries (U - 0.5) exp(2 N(0,1)); alpha ~ U(0.5, 2), beta = 0.5,
-C ~ U[-1, 1); num_moduli = 0 with target 1e-15.  Synthetic seeded data of those shapes and
-distributions (no dataset is involved).  Inputs (about 1.8 GB) exceed the 126 MB L2.
+Workloads are the five BASELINE configurations (tests/workloads.py); the default is C5, the
+largest configuration that fits one B200 (512 problems, 16 shared 4096^2 A operands, operand
+reuse, 36.5 GB of FP64 operands).  C3 and C5 spread one fixed group over the GPUs (strong
+scaling, ggemm_shard_group: reuse components kept whole, no collective on the data path); C2
+gives every GPU its own 64-problem group (weak scaling; rank 0's group is the N = 1 group).
+Inputs exceed the 126 MB L2 in every timed workload but C1.
 
 One JSON line on rank 0.  `value` times K calls with inputs resident in HBM; `e2e` times K
 calls through the same public API with each step's A, B, C copied in from pinned host memory
-and C copied back, steps pipelined over two device buffer sets (step i + 1's copy in overlaps
-step i's compute and copy out).  Multi-GPU (torchrun): the global group has 64 problems per rank, partitioned
-by ggemm_shard_group (cost-balanced, no collective on the data path); timing is the max over
-ranks.  `--impl reference` times the reference's host FP64 path (the naive triple loop of its
-tests, restated in oracle/) on all host threads, on a bounded sample of the same workload.
+and C copied back, steps pipelined over two device buffer sets.  `--impl reference` times the
+reference's host FP64 path (the naive triple loop of its tests, restated in oracle/) on all
+host threads, on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -32,107 +33,19 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "tests"))
 
-PHI = 2.0
-SIZES = list(range(128, 2049, 64))
-PROBS_PER_GPU = 64
-SEED = 20261201
+METRIC = "Effective FP64 TFLOP/s (2Σmnk/t) at 1/2/4/8 B200 vs cuBLAS DGEMM; certified %"
+REF_SO = os.path.join(ROOT, "oracle", "_ref", "libggemm_ref.so")
 
 
-# ----------------------------------------------------------------------------- workload
-def c2_shapes(num: int, seed: int = SEED):
-    rng = np.random.default_rng(seed)
-    m = rng.choice(SIZES, num)
-    n = rng.choice(SIZES, num)
-    k = rng.choice(SIZES, num)
-    alpha = rng.uniform(0.5, 2.0, num)
-    return [(int(m[i]), int(n[i]), int(k[i]), float(alpha[i]), 0.5) for i in range(num)]
+def make_workload(name: str, world: int, rank: int):
+    """(whole workload, this rank's workload) -- they differ only for weak scaling (C2)."""
+    import workloads as W
 
-
-def c3_shapes(num: int):
-    """Config C3 of the survey: num problems of 8192^3, alpha = 1, beta = 0 (INT8-bound)."""
-    return [(8192, 8192, 8192, 1.0, 0.0)] * num
-
-
-def fill_phi(t, phi: float, seed: int):
-    """(U - 0.5) * exp(phi * N(0,1)) in place (device generator, deterministic per seed)."""
-    import torch
-
-    g = torch.Generator(device=t.device)
-    g.manual_seed(seed)
-    u = torch.rand(t.shape, generator=g, device=t.device, dtype=torch.float64)
-    if phi == 0.0:
-        t.copy_(u - 0.5)
-    else:
-        z = torch.randn(t.shape, generator=g, device=t.device, dtype=torch.float64)
-        t.copy_((u - 0.5) * torch.exp(phi * z))
-
-
-class Group:
-    """Device buffers of one rank's problems (tight leading dimensions)."""
-
-    def __init__(self, g2, shapes, seeds, device, phi=PHI):
-        import torch
-
-        self.shapes = shapes
-        na = sum(m * k for m, n, k, _, _ in shapes)
-        nb = sum(k * n for m, n, k, _, _ in shapes)
-        nc = sum(m * n for m, n, k, _, _ in shapes)
-        self.na, self.nb, self.nc = na, nb, nc
-        self.A = torch.empty(max(na, 1), dtype=torch.float64, device=device)
-        self.B = torch.empty(max(nb, 1), dtype=torch.float64, device=device)
-        self.C = torch.empty(max(nc, 1), dtype=torch.float64, device=device)
-        self.C0 = torch.empty(max(nc, 1), dtype=torch.float64, device=device)
-        oa = ob = oc = 0
-        entries = []
-        for (m, n, k, alpha, beta), sd in zip(shapes, seeds):
-            fill_phi(self.A[oa:oa + m * k], phi, sd * 4 + 1)
-            fill_phi(self.B[ob:ob + k * n], phi, sd * 4 + 2)
-            fill_phi(self.C0[oc:oc + m * n], 0.0, sd * 4 + 3)
-            self.C0[oc:oc + m * n].mul_(2.0)  # U[-1, 1)
-            entries.append(dict(m=m, n=n, k=k, A=self.A.data_ptr() + 8 * oa, lda=m,
-                                B=self.B.data_ptr() + 8 * ob, ldb=k,
-                                C=self.C.data_ptr() + 8 * oc, ldc=m, alpha=alpha, beta=beta))
-            oa += m * k
-            ob += k * n
-            oc += m * n
-        self.C.copy_(self.C0)
-        self.problems = g2.make_problems(entries)
-        self.num = len(shapes)
-        self.flops = sum(2.0 * m * n * k for m, n, k, _, _ in shapes)
-        self.g2 = g2
-
-    def problems_on(self, A, B, C):
-        """The same problems with their operands in other device buffers of the same sizes."""
-        oa = ob = oc = 0
-        entries = []
-        for m, n, k, alpha, beta in self.shapes:
-            entries.append(dict(m=m, n=n, k=k, A=A.data_ptr() + 8 * oa, lda=m,
-                                B=B.data_ptr() + 8 * ob, ldb=k, C=C.data_ptr() + 8 * oc,
-                                ldc=m, alpha=alpha, beta=beta))
-            oa += m * k
-            ob += k * n
-            oc += m * n
-        return self.g2.make_problems(entries)
-
-    def algorithmic(self, N: int):
-        """Algorithmic bytes / ops of the three stages for moduli count N (per call)."""
-        prep = recon = ops = 0.0
-        for m, n, k, alpha, beta in self.shapes:
-            kp = (k + 31) // 32 * 32
-            prep += 8.0 * (m * k + k * n) + (N + 1) * (m + n) * kp + 16.0 * (m + n)
-            # products read by the reconstruct: N digit bytes + the int32 abs product per entry
-            # (digit layout), or N + 1 int32 products (int32 layout, narrow problems)
-            per_entry = (N + 4.0) if digit_layout(m, n, N) else 4.0 * (N + 1)
-            recon += per_entry * m * n + (8.0 * m * n if beta != 0 else 0) + 8.0 * m * n \
-                + 16.0 * (m + n)
-            ops += 2.0 * m * n * kp * (N + 1)
-        return prep, ops, recon
-
-
-def digit_layout(m: int, n: int, N: int) -> bool:
-    """The library's per-problem product layout choice (digit layout unless it is larger)."""
-    plane = ((n + 31) // 32 * m * 32 + 255) // 256 * 256
-    return (N + 4) * plane <= 4 * (N + 1) * ((m * n + 63) // 64 * 64)
+    if name == "c2":
+        mine = W.c2(64, W.C2_SEED + rank)
+        return mine, mine
+    wl = W.CONFIGS[name]()
+    return wl, wl
 
 
 # ------------------------------------------------------------------------------ helpers
@@ -227,39 +140,210 @@ def int8_peak_tops(torch):
     return 2.0 * 8192 ** 3 / best / 1e12
 
 
-def traffic_from_profiles(kernel: str):
-    """DRAM bytes per launch of `kernel` on the bench workload from profiles/dram_traffic.txt
-    (lines: <kernel> <bytes_per_launch> <how>), or None."""
+def traffic_from_profiles(kernel: str, workload: str):
+    """DRAM bytes per launch of `kernel` on `workload` from profiles/dram_traffic.txt
+    (lines: <kernel> <workload> <bytes_per_launch> <how>), or None."""
     path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
     try:
         with open(path) as f:
             for line in f:
                 parts = line.split()
-                if len(parts) >= 2 and parts[0] == kernel and not line.startswith("#"):
-                    return float(parts[1])
+                if line.startswith("#") or len(parts) < 3:
+                    continue
+                if parts[0] == kernel and parts[1] == workload:
+                    return float(parts[2])
     except OSError:
         pass
     return None
 
 
-def cpu_reference(oracle, shapes, target_s=12.0, threads=0):
-    """Naive FP64 triple loop on host threads over a column sample of every problem.
-    Returns (TFLOP/s, threads, sample description)."""
+def moduli_of(g2, grp, cfg, path):
+    """Moduli count the planner gives each problem (0 for native routes)."""
+    num = grp.num
+    route = (ctypes.c_int * max(1, num))()
+    nmod = (ctypes.c_int * max(1, num))()
+    tile = (ctypes.c_int * max(1, num))()
+    rc = g2.lib.ggemm_stage_plan(grp.problems, num, ctypes.byref(cfg), path, 148, 36e12, 2.5e15,
+                                 6.0e12, 32.0 ** 3, 16.0, route, nmod, tile)
+    if rc != 0:
+        raise RuntimeError(f"ggemm_stage_plan rc={rc}")
+    return [nmod[i] if route[i] == 0 else 0 for i in range(num)]
+
+
+def digit_layout(m: int, n: int, N: int) -> bool:
+    """The library's per-problem product layout choice (digit layout unless it is larger)."""
+    plane = ((n + 31) // 32 * m * 32 + 255) // 256 * 256
+    return (N + 4) * plane <= 4 * (N + 1) * ((m * n + 63) // 64 * 64)
+
+
+def align(x, a=256):
+    return (x + a - 1) // a * a
+
+
+def img_bytes(g2, rows, k, N):
+    return (N + 1) * align(g2.img_plane_bytes(rows, k))
+
+
+def pool_need(g2, grp, nmods, reuse: bool):
+    """Bytes of residue images and products one chunk of the whole group needs."""
+    a_seen, b_seen = set(), set()
+    need = 0
+    for p, N in zip(grp.pieces, nmods):
+        if N <= 0:
+            continue
+        it = grp.wl.items[p.src]
+        akey = it.a if reuse else ("p", p.src, p.col0)
+        bkey = it.b if reuse else ("p", p.src, p.col0)
+        if akey not in a_seen:
+            a_seen.add(akey)
+            need += img_bytes(g2, it.m, it.k, N)
+        if bkey not in b_seen:
+            b_seen.add(bkey)
+            need += img_bytes(g2, p.n, it.k, N)
+        if digit_layout(it.m, p.n, N):
+            need += align(N * g2.digit_plane_bytes(it.m, p.n) + 4 * g2.digit_plane_bytes(it.m, p.n))
+        else:
+            need += align(4 * (N + 1) * ((it.m * p.n + 63) // 64 * 64))
+    return need + (64 << 20)
+
+
+def algorithmic(grp, nmods, reuse: bool):
+    """Algorithmic bytes of prep and reconstruct and INT8 ops of the GEMM, per call."""
+    prep = recon = ops = 0.0
+    a_seen, b_seen = set(), set()
+    for p, N in zip(grp.pieces, nmods):
+        if N <= 0:
+            continue
+        it = grp.wl.items[p.src]
+        m, n, k = it.m, p.n, it.k
+        kp = (k + 31) // 32 * 32
+        akey = it.a if reuse else ("p", p.src, p.col0)
+        bkey = it.b if reuse else ("p", p.src, p.col0)
+        if akey not in a_seen:
+            a_seen.add(akey)
+            prep += 8.0 * m * k + (N + 1) * m * kp + 16.0 * m
+        if bkey not in b_seen:
+            b_seen.add(bkey)
+            prep += 8.0 * k * n + (N + 1) * n * kp + 16.0 * n
+        per_entry = (N + 4.0) if digit_layout(m, n, N) else 4.0 * (N + 1)
+        recon += per_entry * m * n + (8.0 * m * n if it.beta != 0 else 0) + 8.0 * m * n \
+            + 16.0 * (m + n)
+        ops += 2.0 * m * n * kp * (N + 1)
+    return prep, ops, recon
+
+
+class RefLib:
+    """The reference library (its own sources built for sm_100a into oracle/_ref) through its
+    public API: ggemm_create_ex / ggemm_grouped_dgemm / ggemm_destroy."""
+
+    def __init__(self):
+        L = ctypes.CDLL(REF_SO)
+        L.ggemm_create_ex.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+                                      ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                                      ctypes.c_void_p, ctypes.c_int]
+        L.ggemm_create_ex.restype = ctypes.c_int
+        L.ggemm_grouped_dgemm.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        L.ggemm_grouped_dgemm.restype = ctypes.c_int
+        L.ggemm_destroy.argtypes = [ctypes.c_void_p]
+        self.L = L
+
+
+def ref_calls(wl, grp):
+    """Sub-groups for the reference library, each small enough for its handle: the reference
+    sizes A/B residues as 21 planes x 2 x the summed element budgets and C32 as 21 x 4 bytes per
+    C entry (src/ggemm.cu:228-341), so a group is cut at reuse-component boundaries (C5) or
+    whenever that estimate passes 48 GB."""
+    cap = 48e9
+    out, cur, ca, cb, cc = [], [], 0, 0, 0
+    last_a = None
+    for i, p in enumerate(grp.pieces):
+        it = wl.items[p.src]
+        a, b, c = it.m * it.k, it.k * p.n, it.m * p.n
+        est = 42.0 * (ca + a) + 42.0 * (cb + b) + 84.0 * (cc + c)
+        boundary = cur and ((wl.path_name == "emu_grouped_reuse" and it.a != last_a) or est > cap)
+        if boundary:
+            out.append(cur)
+            cur, ca, cb, cc = [], 0, 0, 0
+        cur.append(i)
+        ca, cb, cc = ca + a, cb + b, cc + c
+        last_a = it.a
+    if cur:
+        out.append(cur)
+    return out
+
+
+def time_reference_library(g2, wl, grp, cfg, path, stream, steps, torch):
+    """Effective TFLOP/s of the reference library on the same device buffers (its own handle,
+    same path and configuration), CUDA events on the same stream.  Sub-groups (ref_calls) run
+    one after another, each with its own handle created and warmed up outside the timed region;
+    a step's time is the sum of its sub-group calls."""
+    if not os.path.exists(REF_SO):
+        return {"value": None, "unavailable": "oracle/_ref/libggemm_ref.so not built"}
+    ref = RefLib()
+    subs = ref_calls(wl, grp)
+    entries = grp.entries_on(grp.A, grp.B, grp.C)
+    reps = max(1, min(steps, 3))
+    per_step = 0.0
+    for sub in subs:
+        probs = g2.make_problems([entries[i] for i in sub])
+        ta = sum(entries[i]["m"] * entries[i]["k"] for i in sub) + 1
+        tb = sum(entries[i]["k"] * entries[i]["n"] for i in sub) + 1
+        tc = sum(entries[i]["m"] * entries[i]["n"] for i in sub) + 1
+        h = ctypes.c_void_p()
+        rc = ref.L.ggemm_create_ex(ctypes.byref(h), len(sub), ta, tb, tc,
+                                   ctypes.c_void_p(stream), wl.min_k)
+        if rc != 0:
+            return {"value": None, "unavailable": f"reference ggemm_create_ex rc={rc}"}
+        try:
+            for r in range(reps + 1):  # one warm-up call, then reps timed calls
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                rc = ref.L.ggemm_grouped_dgemm(h, path, ctypes.addressof(cfg),
+                                               ctypes.addressof(probs), len(sub), None)
+                s1.record()
+                s1.synchronize()
+                if rc != 0:
+                    return {"value": None, "unavailable": f"reference ggemm_grouped_dgemm rc={rc}"}
+                if r > 0:
+                    per_step += s0.elapsed_time(s1) / 1e3 / reps
+        finally:
+            torch.cuda.synchronize()
+            ref.L.ggemm_destroy(h)
+    return {"value": grp.flops / per_step / 1e12, "unit": "TFLOP/s", "calls_per_step": len(subs),
+            "ms_per_step": per_step * 1e3,
+            "how": "oracle/_ref/libggemm_ref.so (reference sources built for sm_100a), same device "
+                   "buffers, path and config, mean of " + str(reps) + " timed steps; " + (
+                       f"{len(subs)} calls per step (its handle cannot hold the whole group)"
+                       if len(subs) > 1 else "one call per step")}
+
+
+def cpu_reference(oracle, shapes, target_s=12.0, threads=0, a_limit=2**26):
+    """Naive FP64 triple loop (the reference's host FP64 path) on host threads over a column
+    sample of the group.  shapes: (m, n, k, alpha, beta, a_id) per problem; problems sharing an
+    a_id share their A matrix.  Problems are taken in order while their A data stays below
+    a_limit elements.  Returns (TFLOP/s, threads, sample description)."""
     rng = np.random.default_rng(7)
-    data = []
-    for m, n, k, alpha, beta in shapes:
-        A = rng.random(m * k) - 0.5
-        B = rng.random(k * n) - 0.5
-        C = rng.random(m * n) - 0.5
-        data.append((m, n, k, alpha, beta, A, B, C))
+    a_mats, data, a_elems = {}, [], 0
+    for m, n, k, alpha, beta, aid in shapes:
+        if aid not in a_mats:
+            if data and a_elems + m * k > a_limit:
+                break
+            a_mats[aid] = rng.random(m * k) - 0.5
+            a_elems += m * k
+        data.append((m, n, k, alpha, beta, a_mats[aid]))
     nthreads = threads if threads > 0 else oracle.L.ozo_max_threads()
 
     def run(cols):
         flops = 0.0
-        t0 = time.perf_counter()
-        for m, n, k, alpha, beta, A, B, C in data:
+        bufs = []
+        for m, n, k, alpha, beta, A in data:
             c = min(n, cols)
-            oracle.dgemm_naive(m, n, k, alpha, A, m, B, k, beta, C, m, 0, c, nthreads)
+            bufs.append((rng.random(k * c) - 0.5, rng.random(m * c) - 0.5))
+        t0 = time.perf_counter()
+        for (m, n, k, alpha, beta, A), (B, C) in zip(data, bufs):
+            c = min(n, cols)
+            oracle.dgemm_naive(m, c, k, alpha, A, m, B, k, beta, C, m, 0, c, nthreads)
             flops += 2.0 * m * c * k
         return flops, time.perf_counter() - t0
 
@@ -271,23 +355,36 @@ def cpu_reference(oracle, shapes, target_s=12.0, threads=0):
     scale = max(1.0, target_s / max(dt, 1e-6))
     cols = int(min(4096, cols * scale))
     flops, dt = run(cols)
-    sample = (f"first {cols} columns of each of the {len(shapes)} problems "
+    sample = (f"first {cols} columns of {len(data)} of the {len(shapes)} problems "
               f"({flops / 2e9:.1f} GFMA, {dt:.1f} s)")
     return flops / dt / 1e12, nthreads, sample
+
+
+def config_of(wl, world):
+    return {"workload": wl.describe, "path": wl.path_name,
+            "parallelism": (f"group sharded over {world} GPU(s) by ggemm_shard_group, no collective"
+                            if wl.scaling == "strong" else
+                            f"one group per GPU on {world} GPU(s), no collective")}
 
 
 # --------------------------------------------------------------------------------- arms
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
     import g2util
 
+    wl, _ = make_workload(args.workload, world, 0)
     oracle = g2util.Oracle()
-    shapes = c2_shapes(PROBS_PER_GPU * args.gpus)
+    shapes = [(it.m, it.n, it.k, it.alpha, it.beta, it.a) for it in wl.items]
+    if wl.scaling == "weak":  # the whole job: every rank's group
+        for r in range(1, world):
+            w2, _ = make_workload(args.workload, world, r)
+            shapes += [(it.m, it.n, it.k, it.alpha, it.beta, (r, it.a)) for it in w2.items]
     target = max(1.0, 60.0 / max(1, args.steps + args.warmup))
     for _ in range(args.warmup):
-        cpu_reference(oracle, shapes, target_s=min(target, 5.0))
+        cpu_reference(oracle, shapes, target_s=min(target, 3.0))
     vals = []
     t0 = time.perf_counter()
     last = None
@@ -296,14 +393,13 @@ def run_reference_arm(args):
         vals.append(last[0])
     wall = time.perf_counter() - t0
     v = float(np.median(vals))
-    flops = sum(2.0 * m * n * k for m, n, k, _, _ in shapes)
+    flops = sum(2.0 * s[0] * s[1] * s[2] for s in shapes)
     line = {
-        "impl": "reference", "metric": "effective FP64 TFLOP/s (2*sum(mnk)/t)", "value": v,
-        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": flops / (v * 1e12) * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "C2: G=64*N ragged m,n,k in {128..2048 step 64}, phi=2, "
-                               "alpha~U(0.5,2), beta=0.5", "path": "host FP64 triple loop"},
+        "impl": "reference", "metric": METRIC, "value": v,
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": flops / (v * 1e12) * 1e3, "higher_is_better": True,
+        "scaling": wl.scaling, "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": dict(config_of(wl, world), path="host FP64 triple loop (reference tests)"),
         "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": last[1], "kind": "port",
                          "sample": last[2]},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -318,13 +414,13 @@ def run_ours(args):
     import torch.distributed as dist
 
     import g2util
+    import workloads as W
 
     g2 = g2util.load_pkg()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        args.gpus = world
+    args.gpus = world
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -333,57 +429,52 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
 
-    # global group, then this rank's shard
-    c3 = args.workload == "c3"
-    gshapes = c3_shapes(args.problems * world) if c3 else c2_shapes(args.problems * world)
-    if world > 1:
-        logical = g2.make_problems([dict(m=m, n=n, k=k, A=0x1000 * (i + 1), lda=m,
-                                         B=0x100000000 * (i + 1), ldb=k,
-                                         C=0x10000000000 * (i + 1), ldc=m, alpha=a, beta=b)
-                                    for i, (m, n, k, a, b) in enumerate(gshapes)])
-        subs, shard, src = g2.shard_group(logical, len(gshapes), world)
-        mine = [i for i in range(len(shard)) if shard[i] == rank]
-        shapes = []
-        seeds = []
-        for i in mine:
-            p = subs[i]
-            shapes.append((p.m, p.n, p.k, p.alpha, p.beta))
-            seeds.append(SEED + 1000 * src[i] + (p.C - logical[src[i]].C) // 8)
-    else:
-        shapes = gshapes
-        seeds = [SEED + 1000 * i for i in range(len(shapes))]
-    stream = torch.cuda.Stream(device=dev)
-    torch.cuda.set_stream(stream)
-    grp = Group(g2, shapes, seeds, dev, phi=0.5 if c3 else PHI)
-    torch.cuda.synchronize()
-    sptr = stream.cuda_stream
-    handle = g2.Handle(max(1, grp.num), grp.na, grp.nb, grp.nc, stream=sptr)
-    cfg = g2.config(num_moduli=16 if c3 else 0, target_rel_err=1e-15, allow_fallback=1)
-
-    def call(path=g2.PATH_EMU_GROUPED):
-        rc, st = handle.grouped_dgemm(path, cfg, grp.problems, grp.num)
-        if rc != 0:
-            raise RuntimeError(f"ggemm_grouped_dgemm rc={rc}")
-        return st
-
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
+    def reduce(x: float, op) -> float:
         if world == 1:
             return x
         t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=op)
         return float(t.item())
 
-    def total_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+    def max_over_ranks(x):
+        return reduce(x, dist.ReduceOp.MAX if world > 1 else None)
+
+    def total_over_ranks(x):
+        return reduce(x, dist.ReduceOp.SUM if world > 1 else None)
+
+    wl_all, wl = make_workload(args.workload, world, rank)
+    pieces = (W.shard_pieces(g2, wl, world, rank) if wl.scaling == "strong"
+              else W.shard_pieces(g2, wl, 1, 0))
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    grp = W.DeviceGroup(g2, wl, pieces, dev)
+    torch.cuda.synchronize()
+    sptr = stream.cuda_stream
+    path = W.path_id(g2, wl.path_name)
+    cfg = g2.config(num_moduli=wl.num_moduli, target_rel_err=wl.target_rel_err,
+                    allow_fallback=wl.allow_fallback)
+    reuse = path == g2.PATH_EMU_GROUPED_REUSE
+    nmods = moduli_of(g2, grp, cfg, path) if grp.num else []
+    # a pool that holds the whole call in one chunk (stage events need a single chunk), at most
+    # 55 % of the device
+    total_mem = torch.cuda.get_device_properties(local).total_memory
+    need = pool_need(g2, grp, nmods, reuse)
+    os.environ["GGEMM_WORKSPACE_FRACTION"] = str(min(0.55, need / total_mem + 0.002))
+    handle = g2.Handle(max(1, grp.num), grp.budget[0] + 1, grp.budget[1] + 1, grp.budget[2] + 1,
+                       stream=sptr, min_k=wl.min_k)
+
+    def call(p=path, probs=None):
+        if grp.num == 0:
+            return g2.Stats()
+        rc, st = handle.grouped_dgemm(p, cfg, grp.problems if probs is None else probs, grp.num)
+        if rc != 0:
+            raise RuntimeError(f"ggemm_grouped_dgemm rc={rc}")
+        return st
 
     # ---------------------------------------------------------------- device-resident timing
     for _ in range(args.warmup):
@@ -411,35 +502,27 @@ def run_ours(args):
     clk = clocks.stop()
     handle.set_stage_events(None)
     elapsed = t_start.elapsed_time(t_stop) / 1e3
+    # per-stage times (recorded by the library when the call runs as one chunk)
     stage_ms = np.array([[es[0].elapsed_time(es[1]), es[1].elapsed_time(es[2]),
                           es[2].elapsed_time(es[3])] for es in ev]).mean(axis=0)
+    if not all(x > 0 for x in stage_ms):
+        stage_ms = np.array([float("nan")] * 3)
     status = handle.device_status()
     if status != 0:
         raise RuntimeError(f"device status {status}")
     t_max = max_over_ranks(elapsed)
     flops_all = total_over_ranks(grp.flops)
     value = flops_all * args.steps / t_max / 1e12
-
+    prep_b, gemm_ops, recon_b = algorithmic(grp, nmods, reuse)
     if args.quick:
         line = {"quick": True, "workload": args.workload, "value": value, "unit": "TFLOP/s",
-                "ms_per_step": t_max / args.steps * 1e3,
+                "ms_per_step": t_max / args.steps * 1e3, "n_gpus": world,
                 "stage_ms": [float(x) for x in stage_ms], "problems_per_gpu": grp.num,
-                "moduli": nmod}
-        if c3:  # cuBLAS DGEMM on the same data, and the GEMM stage's INT8 rate
-            for _ in range(2):
-                call(g2.PATH_NATIVE_GROUPED)
-            barrier()
-            n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            n0.record(stream)
-            for _ in range(args.steps):
-                call(g2.PATH_NATIVE_GROUPED)
-            n1.record(stream)
-            barrier()
-            line["cublas_dgemm_tflops"] = flops_all * args.steps / max_over_ranks(
-                n0.elapsed_time(n1) / 1e3) / 1e12
-            ops = sum(2.0 * m * n * ((k + 31) // 32 * 32) * (nmod + 1)
-                      for m, n, k, _, _ in grp.shapes)
-            line["gemm_int8_tops"] = ops / (stage_ms[1] / 1e3) / 1e12
+                "moduli": nmod, "launches_per_call": launches_per_call,
+                "gemm_int8_tops": gemm_ops / (stage_ms[1] / 1e3) / 1e12 if stage_ms[1] > 0 else None,
+                "prep_gbs": prep_b / (stage_ms[0] / 1e3) / 1e9 if stage_ms[0] > 0 else None,
+                "recon_gbs": recon_b / (stage_ms[2] / 1e3) / 1e9 if stage_ms[2] > 0 else None,
+                "clocks": clk}
         if rank == 0:
             print(json.dumps(line), flush=True)
         handle.close()
@@ -449,17 +532,18 @@ def run_ours(args):
         return 0
 
     # ------------------------------------------------------------------- end-to-end timing
-    # Every step copies its inputs A, B, C from pinned host memory, runs the public call and
-    # copies C back.  Steps are pipelined over two device buffer sets and three streams, as a
-    # serving loop would run them: step i + 1's host->device copy overlaps step i's compute
-    # and device->host copy.
+    # Every step copies its inputs A, B (each unique operand once) and C from pinned host memory,
+    # runs the public call and copies C back.  Steps are pipelined over two device buffer sets
+    # and three streams, as a serving loop would run them: step i + 1's host->device copy
+    # overlaps step i's compute and device->host copy.
+    c_in = any(it.beta != 0.0 for it in wl.items)
     hA = torch.empty(grp.A.shape, dtype=torch.float64, pin_memory=True)
     hB = torch.empty(grp.B.shape, dtype=torch.float64, pin_memory=True)
-    hC0 = torch.empty(grp.C0.shape, dtype=torch.float64, pin_memory=True)
+    hC0 = torch.empty(grp.C.shape, dtype=torch.float64, pin_memory=True)
     hC = torch.empty(grp.C.shape, dtype=torch.float64, pin_memory=True)
     hA.copy_(grp.A)
     hB.copy_(grp.B)
-    hC0.copy_(grp.C0)
+    hC0.copy_(grp.C)
     bufs = [(grp.A, grp.B, grp.C, grp.problems)]
     A2, B2, C2 = torch.empty_like(grp.A), torch.empty_like(grp.B), torch.empty_like(grp.C)
     bufs.append((A2, B2, C2, grp.problems_on(A2, B2, C2)))
@@ -479,12 +563,11 @@ def run_ours(args):
             s_in.wait_event(ev_free[b])  # step i - 2 is done with this buffer set
             A.copy_(hA, non_blocking=True)
             B.copy_(hB, non_blocking=True)
-            C.copy_(hC0, non_blocking=True)
+            if c_in:
+                C.copy_(hC0, non_blocking=True)
             ev_in[b].record(s_in)
         stream.wait_event(ev_in[b])
-        rc, _ = handle.grouped_dgemm(g2.PATH_EMU_GROUPED, cfg, probs, grp.num)
-        if rc != 0:
-            raise RuntimeError(f"ggemm_grouped_dgemm rc={rc}")
+        call(probs=probs)
         ev_done[b].record(stream)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_done[b])
@@ -503,9 +586,11 @@ def run_ours(args):
     barrier()
     e_elapsed = max_over_ranks(e_start.elapsed_time(e_stop) / 1e3)
     e2e_value = flops_all * args.steps / e_elapsed / 1e12
-    h2d = total_over_ranks((grp.na + grp.nb + grp.nc) * 8.0)
+    h2d = total_over_ranks((grp.na + grp.nb + (grp.nc if c_in else 0)) * 8.0)
     d2h = total_over_ranks(grp.nc * 8.0)
     del hA, hB, hC0, hC, bufs, A2, B2, C2
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
 
     # ------------------------------------------------------- cuBLAS native DGEMM, same data
     for _ in range(2):
@@ -522,28 +607,47 @@ def run_ours(args):
 
     # ------------------------------------------------------------ certified fraction (untimed)
     os.environ["GGEMM_STATS_REPAIR"] = "1"
-    h2 = g2.Handle(max(1, grp.num), grp.na, grp.nb, grp.nc, stream=sptr)
+    handle.close()
+    h2 = g2.Handle(max(1, grp.num), grp.budget[0] + 1, grp.budget[1] + 1, grp.budget[2] + 1,
+                   stream=sptr, min_k=wl.min_k)
     os.environ.pop("GGEMM_STATS_REPAIR", None)
-    rc, st2 = h2.grouped_dgemm(g2.PATH_EMU_GROUPED, cfg, grp.problems, grp.num)
+    st2 = g2.Stats()
+    if grp.num:
+        rc, st2 = h2.grouped_dgemm(path, cfg, grp.problems, grp.num)
+        if rc != 0:
+            raise RuntimeError(f"stats call rc={rc}")
     torch.cuda.synchronize()
     h2.close()
-    entries = total_over_ranks(float(sum(m * n for m, n, k, _, _ in grp.shapes)))
+    entries = total_over_ranks(float(sum(it[0] * it[1] for it in grp.shapes())))
     flagged = total_over_ranks(float(max(0, st2.num_uncertified) + max(0, st2.num_repaired)
                                      + max(0, st2.num_safety_fallback)))
     certified = 100.0 * (1.0 - flagged / max(entries, 1.0))
+    torch.cuda.empty_cache()
+
+    # ------------------------------------- the reference library built for sm_100a, same data
+    refv = None
+    if not args.no_ref_lib:
+        try:
+            refv = time_reference_library(g2, wl, grp, cfg, path, sptr, args.steps, torch)
+        except Exception as e:  # reported, never fatal
+            refv = {"value": None, "unavailable": f"{type(e).__name__}: {e}"}
+        v = refv.get("value")
+        per = max_over_ranks(grp.flops / (v * 1e12) if v else 0.0)
+        refv["value"] = (flops_all / per / 1e12) if v and per > 0 else None
+    torch.cuda.empty_cache()
 
     # ------------------------------------------------------------------------ roofline
     hbm, bf16, peak_kind = measured_peaks()
     try:
-        int8 = int8_peak_tops(torch) if rank == 0 else None
+        int8 = int8_peak_tops(torch)
     except RuntimeError:
         int8 = None
-    prep_b, gemm_ops, recon_b = grp.algorithmic(nmod)
     stages = {
         "prep_kernel": {"ms": float(stage_ms[0]), "bound": "hbm", "unit": "GB/s",
                         "achieved": prep_b / (stage_ms[0] / 1e3) / 1e9, "peak": hbm,
                         "algorithmic_bytes": prep_b},
-        "gemm_kernel": {"ms": float(stage_ms[1]), "bound": "tensor", "unit": "TOP/s",
+        "gemm_kernel": {"ms": float(stage_ms[1]), "bound": "tensor", "unit": "TFLOP/s",
+                        "ops": "int8 (TOP/s)",
                         "achieved": gemm_ops / (stage_ms[1] / 1e3) / 1e12, "peak": int8,
                         "algorithmic_ops": gemm_ops},
         "recon_kernel": {"ms": float(stage_ms[2]), "bound": "hbm", "unit": "GB/s",
@@ -554,40 +658,48 @@ def run_ours(args):
         v_["frac"] = (v_["achieved"] / v_["peak"]) if v_["peak"] else None
     dom = max(stages, key=lambda s: stages[s]["ms"])
     d = stages[dom]
-    traffic = traffic_from_profiles(dom)
     roofline = {"kernel": dom, "bound": d["bound"], "achieved": d["achieved"], "peak": d["peak"],
-                "unit": d["unit"], "frac": d["frac"], "traffic": traffic,
+                "unit": d["unit"], "frac": d["frac"],
+                "traffic": traffic_from_profiles(dom, args.workload),
                 "peak_source": (f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if d["bound"] == "hbm"
-                                else "cuBLASLt int8 8192^3 measured in this run")}
+                                else "cuBLASLt INT8 8192^3 (torch._int_mm) measured in this run; "
+                                     f"2 x measured bf16 = {2 * bf16:.0f}")}
+    # INT8-roofline-implied bound on the metric: INT8 peak x sum 2mnk / sum 2mn Kp (N+1)
+    fl = sum(2.0 * s[0] * s[1] * s[2] for s, N in zip(grp.shapes(), nmods) if N > 0)
+    bound = {"int8_implied_tflops": (int8 * fl / gemm_ops) * (flops_all / max(grp.flops, 1))
+             if int8 and gemm_ops else None,
+             "how": "in-run cuBLASLt INT8 x sum 2mnk / sum 2mn Kp (N+1) (abs plane counted)"}
+    if bound["int8_implied_tflops"]:
+        bound["frac"] = value / bound["int8_implied_tflops"]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         oracle = g2util.Oracle()
-        v, cores, sample = cpu_reference(oracle, grp.shapes, target_s=args.cpu_seconds)
+        shp = [(it.m, it.n, it.k, it.alpha, it.beta, it.a) for it in wl.items]
+        v, cores, sample = cpu_reference(oracle, shp, target_s=args.cpu_seconds)
         cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
 
     if rank == 0:
         line = {
-            "metric": "effective FP64 TFLOP/s (2*sum(mnk)/t), EMU_GROUPED vs cuBLAS DGEMM",
+            "metric": METRIC,
             "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
             "dtype": "f64", "data": "synthetic",
-            "config": {"workload": "C2: G=64 per GPU, m,n,k uniform in {128..2048 step 64}, "
-                                   "phi=2, alpha~U(0.5,2), beta=0.5, C~U[-1,1), "
-                                   "num_moduli=0 target 1e-15",
-                       "path": "EMU_GROUPED (repair COUNT)", "moduli": nmod,
-                       "problems_per_gpu": grp.num, "l2": "inputs 1.8 GB/GPU > 126 MB L2",
-                       "parallelism": f"group sharded over {world} GPU(s), no collective"},
+            "config": dict(config_of(wl_all, world), moduli=nmod, problems_rank0=grp.num,
+                           l2=("inputs of every step exceed the 126 MB L2"
+                               if (grp.na + grp.nb) * 8 > 126e6 else "inputs fit L2")),
             "e2e": {"value": e2e_value, "unit": "TFLOP/s",
                     "schedule": "2 buffer sets; copy in / call / copy out on 3 streams",
-                    "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": roofline,
             "stages": stages,
             "cublas_dgemm": {"value": native_value, "unit": "TFLOP/s",
                              "path": "NATIVE_GROUPED (cublasDgemmGroupedBatched)"},
             "speedup_vs_cublas": value / native_value,
+            "ref_ggemm_sm100a": refv,
+            "speedup_vs_ref_ggemm": (value / refv["value"]) if refv and refv.get("value") else None,
+            "int8_bound": bound,
             "certified_pct": certified,
             "cpu_baseline": cpu,
             "clocks": clk,
@@ -596,7 +708,6 @@ def run_ours(args):
                       "int8_tops_cublaslt": int8},
         }
         print(json.dumps(line), flush=True)
-    handle.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -609,25 +720,18 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c5",
+                    help="BASELINE configuration (tests/workloads.py); c5 is the headline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-lib", action="store_true",
+                    help="skip timing the reference library built for sm_100a")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--problems", type=int, default=PROBS_PER_GPU,
-                    help="problems per GPU (64 = the C2 workload; fewer for profiling)")
-    ap.add_argument("--workload", choices=["c2", "c3"], default="c2",
-                    help="c2: the bench line's workload; c3: 8192^3 problems, N = 16, "
-                         "--quick only (device timing, cuBLAS DGEMM beside it)")
     ap.add_argument("--quick", action="store_true",
                     help="device-resident timing only (profiling runs): no e2e, cuBLAS, "
-                         "certified or CPU legs")
+                         "certified, reference or CPU legs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload == "c3":
-        if args.impl == "reference":
-            ap.error("--workload c3 times this library only")
-        args.quick = True
-        if args.problems == PROBS_PER_GPU:
-            args.problems = 8
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_ours(args)

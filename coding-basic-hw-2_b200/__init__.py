@@ -178,6 +178,8 @@ def _load():
         "ggemm_stage_crt_tables": (c_size_t, [c_void_p, c_size_t]),
         "ggemm_stage_error_bound": (c_double, [c_int, c_int]),
         "ggemm_dgemm_noalloc": (c_int, [POINTER(Problem), c_int, c_int, c_void_p]),
+        "ggemm_dgemm_noalloc_status": (c_int, [c_void_p]),
+        "ggemm_stage_wait_probe": (c_int, [c_void_p, c_longlong, c_void_p]),
         "ggemm_device_count": (c_int, []),
         "ggemm_version": (c_char_p, []),
     }

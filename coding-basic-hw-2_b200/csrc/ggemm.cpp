@@ -147,10 +147,10 @@ void print_ws_diag(ggemm_handle_t h, const ggemm_problem_t& p, int N) {
   h->ws_diag_printed = 1;
   std::fprintf(stderr,
                "[ggemm] GGEMM_ERR_WORKSPACE: one problem (m=%d n=%d k=%d, %d moduli) needs "
-               "%zu + %zu residue bytes and %zu product bytes; the handle holds %zu + %zu "
-               "and %zu bytes (create with larger budgets or min_k <= %d)\n",
+               "%zu + %zu residue bytes and %zu product bytes; the handle's pool holds %zu "
+               "bytes (create with larger budgets or min_k <= %d)\n",
                p.m, p.n, p.k, N, img_bytes(p.m, p.k, N), img_bytes(p.n, p.k, N),
-               4 * product_elems(p.m, p.n, N), h->imgA_cap, h->imgB_cap, 4 * h->c32_cap, p.k);
+               4 * product_elems(p.m, p.n, N), h->pool_cap, p.k);
 }
 
 }  // namespace
@@ -225,13 +225,18 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
   for (int u = 0; u < c.num_ua; ++u) h->ua_chunk[u] = -1;
   for (int u = 0; u < c.num_ub; ++u) h->ub_chunk[u] = -1;
 
-  // chunks: consecutive emulated problems whose images and products fit the workspace
+  // chunks: consecutive emulated problems whose images and products fit the workspace pool
+  // (A images, then B images, then products, each region 256-byte aligned)
   h->chunks.clear();
   {
     size_t ia = 0, ib = 0, wa = 0, wb = 0, cc = 0;
     Chunk cur{};
     cur.first = 0;
     cur.count = 0;
+    auto close = [&](Chunk& ch) {
+      ch.base_b = align_up(ia, kAlign);
+      ch.base_c = align_up(ch.base_b + ib, kAlign);
+    };
     for (int j = 0; j < c.ne; ++j) {
       const int g = emu[j];
       const ggemm_problem_t& p = probs[g];
@@ -247,9 +252,10 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         const size_t nwa = new_a ? ws_ints(p.m) : 0;
         const size_t nwb = new_b ? ws_ints(p.n) : 0;
         const size_t ncc = product_elems(p.m, p.n, N);
-        const bool fits = ia + na <= h->imgA_cap && ib + nb <= h->imgB_cap &&
-                          wa + nwa <= h->wsA_cap && wb + nwb <= h->wsB_cap &&
-                          cc + ncc <= h->c32_cap;
+        const size_t bytes = align_up(ia + na, kAlign) + align_up(ib + nb, kAlign) +
+                             4 * (cc + ncc);
+        const bool fits = bytes <= h->pool_cap && wa + nwa <= h->wsA_cap &&
+                          wb + nwb <= h->wsB_cap;
         if (fits && !(chunk_per_problem && cur.count > 0)) {
           if (new_a) {
             h->ua_chunk[ua] = cid;
@@ -274,7 +280,8 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
           print_ws_diag(h, p, N);
           return GGEMM_ERR_WORKSPACE;
         }
-        h->chunks.push_back(cur);  // close the chunk and retry in a fresh one
+        close(cur);  // close the chunk and retry in a fresh one
+        h->chunks.push_back(cur);
         cur = Chunk{};
         cur.first = j;
         cur.count = 0;
@@ -283,7 +290,10 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         (void)attempt;
       }
     }
-    if (cur.count > 0) h->chunks.push_back(cur);
+    if (cur.count > 0) {
+      close(cur);
+      h->chunks.push_back(cur);
+    }
   }
 
   // descriptors
@@ -325,7 +335,7 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         d.k = p.k;
         d.N = h->ua_n[ua];
         d.kind = ch.qscale ? GGEMM_PREP_QSCALED : 0;
-        d.img = h->imgA + h->ua_img[ua];
+        d.img = h->pool + h->ua_img[ua];
         d.plane_bytes = (long long)align_up(ggemm_img_plane_bytes(p.m, p.k), kAlign);
         d.ws = h->wsA + h->ua_ws[ua];
         ++q;
@@ -340,7 +350,7 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         d.k = p.k;
         d.N = h->ub_n[ub];
         d.kind = 1;
-        d.img = h->imgB + h->ub_img[ub];
+        d.img = h->pool + ch.base_b + h->ub_img[ub];
         d.plane_bytes = (long long)align_up(ggemm_img_plane_bytes(p.n, p.k), kAlign);
         d.ws = h->wsB + h->ub_ws[ub];
         ++q;
@@ -385,9 +395,9 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       const int N = plan[g].num_moduli;
       const int ua = h->ua_of[j], ub = h->ub_of[j];
       GemmJob base{};
-      base.A = h->imgA + h->ua_img[ua];
-      base.B = h->imgB + h->ub_img[ub];
-      base.C = h->c32 + h->c32_off[j];
+      base.A = h->pool + h->ua_img[ua];
+      base.B = h->pool + ch.base_b + h->ub_img[ub];
+      base.C = reinterpret_cast<int32_t*>(h->pool + ch.base_c) + h->c32_off[j];
       base.Y = reinterpret_cast<uint8_t*>(base.C);
       base.a_plane = (long long)align_up(ggemm_img_plane_bytes(p.m, p.k), kAlign);
       base.b_plane = (long long)align_up(ggemm_img_plane_bytes(p.n, p.k), kAlign);
@@ -443,7 +453,7 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       d.ldc = p.ldc;
       d.alpha = p.alpha;
       d.beta = p.beta;
-      d.C32 = h->c32 + h->c32_off[j];
+      d.C32 = reinterpret_cast<int32_t*>(h->pool + ch.base_c) + h->c32_off[j];
       d.c_plane = y8 ? (long long)y8_plane_bytes(p.m, p.n) : (long long)c_plane_elems(p.m, p.n);
       d.rs = h->wsA + h->ua_ws[h->ua_of[j]];
       d.cs = h->wsB + h->ub_ws[h->ub_of[j]];
@@ -651,9 +661,7 @@ extern "C" void ggemm_destroy(ggemm_handle_t h) {
   }
   if (h->cublas) cublasDestroy(h->cublas);
   cudaFree(h->cublas_ws);
-  cudaFree(h->imgA);
-  cudaFree(h->imgB);
-  cudaFree(h->c32);
+  cudaFree(h->pool);
   cudaFree(h->wsA);
   cudaFree(h->wsB);
   cudaFree(h->counters);
@@ -712,12 +720,12 @@ extern "C" int ggemm_create_ex(ggemm_handle_t* out, int max_problems, size_t max
       cublasSetMathMode(h->cublas, CUBLAS_DEFAULT_MATH) != CUBLAS_STATUS_SUCCESS)
     FAIL(GGEMM_ERR_CUBLAS);
 
-  // Workspace: the reference's sizing (21 planes, K padding inflation, per-problem slack),
-  // capped at a fraction of device memory; calls that need more run in chunks.
+  // Workspace: the reference's sizing (21 planes, K padding inflation, per-problem slack) as
+  // one pool, capped at a fraction of device memory; calls that need more run in chunks.
   const double infl = std::max(2.0, k_inflation(min_k));
-  size_t want_a = kPlanesMax * ((size_t)std::ceil(infl * (double)max_A) + P * 2048);
-  size_t want_b = kPlanesMax * ((size_t)std::ceil(infl * (double)max_B) + P * 2048);
-  size_t want_c = kPlanesMax * (max_C + P * 64);  // int32 elements
+  double want = kPlanesMax * (std::ceil(infl * (double)max_A) + (double)P * 2048) +
+                kPlanesMax * (std::ceil(infl * (double)max_B) + (double)P * 2048) +
+                4.0 * kPlanesMax * ((double)max_C + (double)P * 64);
   {
     size_t free_b = 0, total_b = 0;
     cudaMemGetInfo(&free_b, &total_b);
@@ -726,23 +734,12 @@ extern "C" int ggemm_create_ex(ggemm_handle_t* out, int max_problems, size_t max
       const double v = std::atof(e);
       if (v > 0.0 && v <= 0.95) frac = v;
     }
-    const double budget = frac * (double)total_b;
-    const double want = (double)want_a + (double)want_b + 4.0 * (double)want_c;
-    if (want > budget && want > 0) {
-      const double s = budget / want;
-      want_a = (size_t)(want_a * s);
-      want_b = (size_t)(want_b * s);
-      want_c = (size_t)(want_c * s);
-    }
+    want = std::min(want, frac * (double)total_b);
   }
-  h->imgA_cap = align_up(std::max<size_t>(want_a, 1 << 16), kAlign);
-  h->imgB_cap = align_up(std::max<size_t>(want_b, 1 << 16), kAlign);
-  h->c32_cap = align_up(std::max<size_t>(want_c, 1 << 14), 64);
+  h->pool_cap = align_up(std::max<size_t>((size_t)want, 1 << 18), kAlign);
   h->wsA_cap = 4 * max_A + P * 64 + 64;
   h->wsB_cap = 4 * max_B + P * 64 + 64;
-  CUA(cudaMalloc(&h->imgA, h->imgA_cap));
-  CUA(cudaMalloc(&h->imgB, h->imgB_cap));
-  CUA(cudaMalloc(&h->c32, h->c32_cap * sizeof(int32_t)));
+  CUA(cudaMalloc(&h->pool, h->pool_cap));
   CUA(cudaMalloc(&h->wsA, h->wsA_cap * sizeof(int32_t)));
   CUA(cudaMalloc(&h->wsB, h->wsB_cap * sizeof(int32_t)));
   CUA(cudaMalloc(&h->counters, sizeof(DevCounters)));

@@ -46,6 +46,7 @@ struct Chunk {
   int first, count;        // range in emu order
   size_t off_prep, off_prep_prefix, off_jobs, off_job_prefix, off_recon, off_recon_prefix;
   int num_prep, prep_blocks;
+  size_t base_b, base_c;   // byte offsets of the chunk's B images and products in the pool
   PrepSplit prep_split;    // descriptors sorted by prep instance (launch_prep)
   ReconSplit recon_split;  // ... by reconstruct instance (launch_recon)
   bool qscale;  // A images q-scaled (every problem of the chunk in the digit layout)
@@ -65,13 +66,11 @@ struct ggemm_handle_s {
   size_t max_A = 0, max_B = 0, max_C = 0;
   int min_k = 32;
 
-  // device workspace (allocated at create; every call fits into it, in chunks if needed)
-  int8_t* imgA = nullptr;
-  size_t imgA_cap = 0;
-  int8_t* imgB = nullptr;
-  size_t imgB_cap = 0;
-  int32_t* c32 = nullptr;
-  size_t c32_cap = 0;  // int32 elements
+  // device workspace (allocated at create; every call fits into it, in chunks if needed).
+  // One pool per handle holds, per chunk, the A images from offset 0, then the B images, then
+  // the products (Chunk::base_b / base_c), so the split follows each call's shapes.
+  int8_t* pool = nullptr;
+  size_t pool_cap = 0;  // bytes
   int32_t* wsA = nullptr;
   size_t wsA_cap = 0;
   int32_t* wsB = nullptr;
@@ -136,4 +135,7 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
                      int* launches);
 int enqueue_native(ggemm_handle_t h, const ggemm_problem_t* probs, const int* idx, int cnt,
                    bool grouped, int ngroups, const char* d_ptrs, cudaStream_t s, int* launches);
+// Device address of the counter block of ggemm_dgemm_noalloc's scratch on the current device
+// (noalloc.cu; sets the device up on first use).  Returns GGEMM_OK or an error.
+int noalloc_counters(DevCounters** out);
 }  // namespace g2

@@ -1197,6 +1197,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
+// ================================================================== bounded-wait probe
+__global__ void __launch_bounds__(32, 1)
+    wait_probe_kernel(DevCounters* __restrict__ cnt, unsigned long long wait_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    // phase 0 never completes: no thread arrives on `bar`
+    if (!mbar_wait(&bar, 0, global_timer_ns() + wait_ns, &abort))
+      atomicCAS(&cnt->status, 0u, (unsigned)kStatusProbeTimeout);
+  }
+  __syncwarp();
+}
+
 // ======================================================================= reconstruct kernel
 // y mod p for 0 <= y < 2^32, magic = floor(2^32 / p): the estimate undershoots by at most one.
 __device__ __forceinline__ uint32_t mod_p(uint32_t y, uint32_t p, uint32_t magic) {
@@ -1728,6 +1747,13 @@ int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long 
   const long long grid = std::min<long long>(total_tiles, (long long)current_device_sms());
   gemm_kernel<<<(unsigned)grid, kGemmThreads, kGemmSmem, s>>>(d_jobs, d_prefix, num, total_tiles,
                                                               cnt);
+  return (int)cudaGetLastError();
+}
+
+int launch_wait_probe(DevCounters* cnt, unsigned long long wait_ns, cudaStream_t s) {
+  wait_ns = std::min<unsigned long long>(std::max<unsigned long long>(wait_ns, 1000ull),
+                                         1000000000ull);
+  wait_probe_kernel<<<1, 32, 0, s>>>(cnt, wait_ns);
   return (int)cudaGetLastError();
 }
 

@@ -25,6 +25,7 @@ enum : unsigned int {
   kStatusOk = 0,
   kStatusGemmTimeout = 1,  // a residue-GEMM pipeline wait ran past its deadline
   kStatusPrepTimeout = 2,  // a prep residue-MMA wait ran past its deadline
+  kStatusProbeTimeout = 3, // the bounded-wait probe (launch_wait_probe) gave up, as designed
 };
 
 // Digit layout ("Y8", GGEMM_PRODUCTS_DIGITS in ggemm_stages.h) of the products handed from the
@@ -167,6 +168,11 @@ inline void recon_partition(ggemm_recon_desc_t* descs, int num, long long* prefi
   sp->block0[kReconClasses] = blocks;
   prefix[num] = blocks;
 }
+// Bounded-wait probe: one block waits on an mbarrier that nothing arrives on, through the same
+// bounded wait (mbar_wait with a %globaltimer deadline) as the pipeline kernels, gives up after
+// wait_ns and records kStatusProbeTimeout in cnt->status.  It shows the give-up path ends and
+// leaves the context usable, without a fault.  wait_ns is clamped to [1 us, 1 s].
+int launch_wait_probe(DevCounters* cnt, unsigned long long wait_ns, cudaStream_t s);
 // One launch per non-empty class; *launches, when given, is increased by their number.
 int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix,
                  const ReconSplit& sp, int mode, DevCounters* cnt, cudaStream_t s,

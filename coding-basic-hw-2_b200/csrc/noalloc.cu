@@ -12,6 +12,7 @@
 // cudaFree, cudaMemcpy or any allocating library routine.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstddef>
 #include <cstdio>
 #include <mutex>
@@ -53,6 +54,25 @@ __global__ void noalloc_setup_kernel(NoAllocDescs d) {
   }
 }
 
+// C = beta C, not reading C when beta == 0: what ggemm_grouped_dgemm computes for alpha == 0 or
+// k == 0 (its native route).  Block 0 also clears the counters, so the status query reports this
+// call.
+__global__ void noalloc_scale_kernel(double* __restrict__ C, long long ldc, int m, int n,
+                                     double beta) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    DevCounters* c = reinterpret_cast<DevCounters*>(g_noalloc_scratch + kOffCounters);
+    c->nonfinite = c->uncertified = c->repaired = c->safety = 0;
+    c->status = 0;
+  }
+  const long long total = (long long)m * n;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long j = e / m, i = e - j * m;
+    double* c = C + i + j * ldc;
+    *c = beta == 0.0 ? 0.0 : beta * *c;
+  }
+}
+
 std::mutex g_mu;
 unsigned char* g_addr[64] = {nullptr};
 
@@ -80,6 +100,14 @@ int setup_current_device(unsigned char** out) {
 inline size_t up256(size_t x) { return (x + 255) / 256 * 256; }
 
 }  // namespace
+
+int noalloc_counters(DevCounters** out) {
+  unsigned char* base = nullptr;
+  if (int r = setup_current_device(&base)) return r;
+  *out = reinterpret_cast<DevCounters*>(base + kOffCounters);
+  return GGEMM_OK;
+}
+
 }  // namespace g2
 
 using namespace g2;
@@ -106,7 +134,14 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
                    : repair_mode == GGEMM_REPAIR_OFF   ? GGEMM_STAGE_REPAIR_OFF
                    : repair_mode == GGEMM_REPAIR_COUNT ? GGEMM_STAGE_REPAIR_COUNT
                                                        : GGEMM_STAGE_REPAIR_ON;
-  const bool emulate = q.alpha != 0.0;  // alpha == 0: C = beta C without reading A or B
+  if (q.alpha == 0.0 || q.k == 0) {  // C = beta C without reading A or B
+    unsigned char* base = nullptr;
+    if (int r = setup_current_device(&base)) return r;
+    const long long total = (long long)q.m * q.n;
+    const long long blocks = std::min<long long>((total + 255) / 256, 148ll * 8);
+    noalloc_scale_kernel<<<(unsigned)blocks, 256, 0, stream>>>(q.C, q.ldc, q.m, q.n, q.beta);
+    return cudaGetLastError() == cudaSuccess ? GGEMM_OK : GGEMM_ERR_CUDA;
+  }
 
   // scratch layout: counters | descriptors | ws A | ws B | image A | image B | products
   const size_t pa = up256(ggemm_img_plane_bytes(q.m, q.k));
@@ -117,9 +152,9 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
   const size_t off_wa = kOffData;
   const size_t off_wb = off_wa + up256(16 * (size_t)q.m);
   const size_t off_ia = off_wb + up256(16 * (size_t)q.n);
-  const size_t off_ib = off_ia + (emulate ? (size_t)(N + 1) * pa : 0);
-  const size_t off_c = off_ib + (emulate ? (size_t)(N + 1) * pb : 0);
-  const size_t need = off_c + (emulate && q.k > 0 ? prod : 0);
+  const size_t off_ib = off_ia + (size_t)(N + 1) * pa;
+  const size_t off_c = off_ib + (size_t)(N + 1) * pb;
+  const size_t need = off_c + prod;
   if (need > kNoAllocBytes) {
     std::fprintf(stderr,
                  "[ggemm] ggemm_dgemm_noalloc: m=%d n=%d k=%d with %d moduli needs %zu bytes of "
@@ -132,7 +167,7 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
 
   NoAllocDescs d{};
   int nprep = 0, prep_blocks_total = 0;
-  if (emulate) {
+  {
     ggemm_prep_desc_t a{};
     a.X = q.A;
     a.ld = q.lda;
@@ -173,7 +208,7 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
   j.m = q.m;
   j.n = q.n;
   j.ksteps = (q.k + 31) / 32;
-  j.planes = (emulate && q.k > 0) ? N + 1 : 0;
+  j.planes = N + 1;
   set_gemm_tiling(j);
   d.job_prefix[0] = 0;
   d.job_prefix[1] = gemm_tiles(j);
@@ -229,4 +264,13 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
                    rsp, mode, cnt, stream))
     return GGEMM_ERR_NUMERICS;
   return GGEMM_OK;
+}
+
+extern "C" int ggemm_dgemm_noalloc_status(cudaStream_t stream) {
+  DevCounters c{};
+  if (cudaMemcpyFromSymbolAsync(&c, g_noalloc_scratch, sizeof c, kOffCounters,
+                                cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return -1;
+  return (int)c.status;
 }

@@ -174,6 +174,14 @@ extern "C" int ggemm_stage_recon(const ggemm_recon_desc_t* descs, int num, int r
              : GGEMM_OK;
 }
 
+extern "C" int ggemm_stage_wait_probe(void* counters, long long wait_ns, cudaStream_t s) {
+  DevCounters* cnt = static_cast<DevCounters*>(counters);
+  if (!cnt && noalloc_counters(&cnt) != GGEMM_OK) return GGEMM_ERR_CUDA;
+  return launch_wait_probe(cnt, (unsigned long long)(wait_ns > 0 ? wait_ns : 0), s)
+             ? GGEMM_ERR_CUDA
+             : GGEMM_OK;
+}
+
 extern "C" int ggemm_device_count(void) {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess) {

@@ -25,7 +25,8 @@ extern "C" {
 int ggemm_set_stage_events(ggemm_handle_t h, cudaEvent_t* events);
 
 /* Synchronizes the handle's stream and returns the device status word of the handle's kernels
- * (0 = ok, 1 = a residue-GEMM pipeline wait ran past its deadline); -1 on a CUDA error. */
+ * (0 = ok, 1 = a residue-GEMM pipeline wait ran past its deadline, 2 = a prep residue-MMA
+ * wait ran past its deadline); -1 on a CUDA error. */
 int ggemm_device_status(ggemm_handle_t h);
 
 /* Partitions `num` problems over `num_shards` devices.  A problem may be split into column
@@ -50,7 +51,9 @@ int ggemm_shard_group(const ggemm_problem_t* problems, int num, int num_shards,
  * Nothing is allocated: no cudaMalloc / cudaFree, no allocating library routine.
  *   num_moduli: 0 = adaptive (target 1e-15) or a fixed N in [2, 20];
  *   repair_mode: GGEMM_REPAIR_* (default = COUNT, as GGEMM_PATH_EMU_GROUPED).
- * Results equal ggemm_grouped_dgemm(GGEMM_PATH_EMU_GROUPED) of the same problem, bit for bit.
+ * Results equal ggemm_grouped_dgemm(GGEMM_PATH_EMU_GROUPED) of the same problem, bit for bit:
+ * for alpha == 0 or k == 0 both compute C = beta C (C = 0, C not read, when beta == 0), which
+ * the grouped call does through its native route.
  * A problem whose scratch exceeds 64 MiB (about 1130^3 at N = 15) returns GGEMM_ERR_WORKSPACE
  * with a one-line message on stderr, before anything is enqueued; k > 131040 returns
  * GGEMM_ERR_UNSAFE.
@@ -61,6 +64,13 @@ int ggemm_shard_group(const ggemm_problem_t* problems, int num, int num_shards,
  * streams, other host threads) race and must be ordered by the caller. */
 int ggemm_dgemm_noalloc(const ggemm_problem_t* problem, int num_moduli, int repair_mode,
                         cudaStream_t stream);
+
+/* Device status of the last ggemm_dgemm_noalloc call enqueued on this device: synchronizes
+ * `stream` (the stream of that call), then reads the status word in the fixed scratch (no
+ * allocation).  0 = ok; 1 or 2 = a residue-GEMM or prep pipeline wait ran past its deadline, so
+ * that call's C is not valid; -1 on a CUDA error.  The next call clears the word when it starts
+ * on the GPU, so read it before enqueueing another call. */
+int ggemm_dgemm_noalloc_status(cudaStream_t stream);
 
 #ifdef __cplusplus
 }

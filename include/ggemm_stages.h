@@ -140,6 +140,15 @@ int ggemm_stage_gemm(const ggemm_gemm_desc_t* descs, int num, void* scratch,
 int ggemm_stage_recon(const ggemm_recon_desc_t* descs, int num, int repair_mode, void* scratch,
                       size_t scratch_bytes, void* counters, cudaStream_t s);
 
+/* Bounded-wait probe (no counterpart in the reference, whose kernels never wait on one
+ * another): one block waits on an mbarrier that nothing arrives on, through the same bounded
+ * wait the pipeline kernels use, gives up after wait_ns (clamped to [1 us, 1 s]) and sets the
+ * status word of `counters` to 3 if it was 0.  counters == NULL targets the counter block of the
+ * allocation-free entry point (ggemm_dgemm_noalloc, ggemm_ext.h) on the current device.  It lets
+ * a test make a wait run out and check that the host reads the status and the context stays
+ * usable, without a fault.  Returns GGEMM_OK or GGEMM_ERR_CUDA. */
+int ggemm_stage_wait_probe(void* counters, long long wait_ns, cudaStream_t s);
+
 /* Host-only planner seam (replaces ggemm_plan, src/planner.cpp:281-330): plans num problems
  * for the given path with an explicit device model, writing route / moduli / cost-model tile
  * class per problem (route codes of the reference's ggemm_route_t, src/planner.h:7-17).
