@@ -225,8 +225,12 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
   for (int u = 0; u < c.num_ua; ++u) h->ua_chunk[u] = -1;
   for (int u = 0; u < c.num_ub; ++u) h->ub_chunk[u] = -1;
 
-  // chunks: consecutive emulated problems whose images and products fit the workspace pool
-  // (A images, then B images, then products, each region 256-byte aligned)
+  // chunks: consecutive emulated problems whose residue images, products and row / column
+  // workspace fit the pool.  Chunk layout: A images from offset 0, then B images, products,
+  // row workspace and column workspace, each region 256-byte aligned.  A unique operand is
+  // prepared once per chunk that uses it; each problem records where its operands' images and
+  // workspace lie in its own chunk (pa_* / pb_*), and whether it is the problem that prepares
+  // them there (pa_new / pb_new).
   h->chunks.clear();
   {
     size_t ia = 0, ib = 0, wa = 0, wb = 0, cc = 0;
@@ -236,6 +240,8 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
     auto close = [&](Chunk& ch) {
       ch.base_b = align_up(ia, kAlign);
       ch.base_c = align_up(ch.base_b + ib, kAlign);
+      ch.base_wa = align_up(ch.base_c + 4 * cc, kAlign);
+      ch.base_wb = align_up(ch.base_wa + 4 * wa, kAlign);
     };
     for (int j = 0; j < c.ne; ++j) {
       const int g = emu[j];
@@ -253,10 +259,9 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         const size_t nwb = new_b ? ws_ints(p.n) : 0;
         const size_t ncc = product_elems(p.m, p.n, N);
         const size_t bytes = align_up(ia + na, kAlign) + align_up(ib + nb, kAlign) +
-                             4 * (cc + ncc);
-        const bool fits = bytes <= h->pool_cap && wa + nwa <= h->wsA_cap &&
-                          wb + nwb <= h->wsB_cap;
-        if (fits && !(chunk_per_problem && cur.count > 0)) {
+                             align_up(4 * (cc + ncc), kAlign) + align_up(4 * (wa + nwa), kAlign) +
+                             4 * (wb + nwb);
+        if (bytes <= h->pool_cap && !(chunk_per_problem && cur.count > 0)) {
           if (new_a) {
             h->ua_chunk[ua] = cid;
             h->ua_img[ua] = ia;
@@ -271,6 +276,12 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
             ib += nb;
             wb += nwb;
           }
+          h->pa_new[j] = new_a;
+          h->pb_new[j] = new_b;
+          h->pa_img[j] = h->ua_img[ua];
+          h->pa_ws[j] = h->ua_ws[ua];
+          h->pb_img[j] = h->ub_img[ub];
+          h->pb_ws[j] = h->ub_ws[ub];
           h->c32_off[j] = cc;
           cc += ncc;
           ++cur.count;
@@ -300,7 +311,6 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
   BlobWriter bw{hb, 0, h->blob_cap};
   int* order = h->order.data();
   for (Chunk& ch : h->chunks) {
-    const int cid = (int)(&ch - h->chunks.data());
     // The A images of a chunk are q-scaled (GGEMM_PREP_QSCALED) when every problem of the chunk
     // takes the digit layout and has its A image's moduli count: the GEMM epilogue then
     // skips the modular product by q_l.
@@ -310,12 +320,11 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       const int N = plan[emu[j]].num_moduli;
       if (!use_y8(p.m, p.n, N) || h->ua_n[h->ua_of[j]] != N) ch.qscale = false;
     }
-    // prep descriptors: unique A / B operands first placed in this chunk
+    int32_t* wsa = reinterpret_cast<int32_t*>(h->pool + ch.base_wa);
+    int32_t* wsb = reinterpret_cast<int32_t*>(h->pool + ch.base_wb);
+    // prep descriptors: the unique A / B operands this chunk prepares
     int np = 0;
-    for (int j = ch.first; j < ch.first + ch.count; ++j) {
-      if (h->ua_chunk[h->ua_of[j]] == cid) ++np, h->ua_chunk[h->ua_of[j]] = -2 - cid;
-      if (h->ub_chunk[h->ub_of[j]] == cid) ++np, h->ub_chunk[h->ub_of[j]] = -2 - cid;
-    }
+    for (int j = ch.first; j < ch.first + ch.count; ++j) np += h->pa_new[j] + h->pb_new[j];
     ch.num_prep = np;
     ch.off_prep = bw.take((size_t)np * sizeof(ggemm_prep_desc_t), 64);
     ch.off_prep_prefix = bw.take((size_t)(np + 1) * sizeof(int), 16);
@@ -325,8 +334,7 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
     int q = 0, blocks = 0;
     for (int j = ch.first; j < ch.first + ch.count; ++j) {
       const int ua = h->ua_of[j], ub = h->ub_of[j];
-      if (h->ua_chunk[ua] == -2 - cid) {
-        h->ua_chunk[ua] = cid;
+      if (h->pa_new[j]) {
         const ggemm_problem_t& p = probs[h->ua_rep[ua]];
         ggemm_prep_desc_t& d = pd[q];
         d.X = p.A;
@@ -335,13 +343,12 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         d.k = p.k;
         d.N = h->ua_n[ua];
         d.kind = ch.qscale ? GGEMM_PREP_QSCALED : 0;
-        d.img = h->pool + h->ua_img[ua];
+        d.img = h->pool + h->pa_img[j];
         d.plane_bytes = (long long)align_up(ggemm_img_plane_bytes(p.m, p.k), kAlign);
-        d.ws = h->wsA + h->ua_ws[ua];
+        d.ws = wsa + h->pa_ws[j];
         ++q;
       }
-      if (h->ub_chunk[ub] == -2 - cid) {
-        h->ub_chunk[ub] = cid;
+      if (h->pb_new[j]) {
         const ggemm_problem_t& p = probs[h->ub_rep[ub]];
         ggemm_prep_desc_t& d = pd[q];
         d.X = p.B;
@@ -350,9 +357,9 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         d.k = p.k;
         d.N = h->ub_n[ub];
         d.kind = 1;
-        d.img = h->pool + ch.base_b + h->ub_img[ub];
+        d.img = h->pool + ch.base_b + h->pb_img[j];
         d.plane_bytes = (long long)align_up(ggemm_img_plane_bytes(p.n, p.k), kAlign);
-        d.ws = h->wsB + h->ub_ws[ub];
+        d.ws = wsb + h->pb_ws[j];
         ++q;
       }
     }
@@ -393,10 +400,9 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       const int g = emu[j];
       const ggemm_problem_t& p = probs[g];
       const int N = plan[g].num_moduli;
-      const int ua = h->ua_of[j], ub = h->ub_of[j];
       GemmJob base{};
-      base.A = h->pool + h->ua_img[ua];
-      base.B = h->pool + ch.base_b + h->ub_img[ub];
+      base.A = h->pool + h->pa_img[j];
+      base.B = h->pool + ch.base_b + h->pb_img[j];
       base.C = reinterpret_cast<int32_t*>(h->pool + ch.base_c) + h->c32_off[j];
       base.Y = reinterpret_cast<uint8_t*>(base.C);
       base.a_plane = (long long)align_up(ggemm_img_plane_bytes(p.m, p.k), kAlign);
@@ -455,8 +461,8 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       d.beta = p.beta;
       d.C32 = reinterpret_cast<int32_t*>(h->pool + ch.base_c) + h->c32_off[j];
       d.c_plane = y8 ? (long long)y8_plane_bytes(p.m, p.n) : (long long)c_plane_elems(p.m, p.n);
-      d.rs = h->wsA + h->ua_ws[h->ua_of[j]];
-      d.cs = h->wsB + h->ub_ws[h->ub_of[j]];
+      d.rs = wsa + h->pa_ws[j];
+      d.cs = wsb + h->pb_ws[j];
     }
     // descriptors sorted by reconstruct instance (launch_recon)
     recon_partition(rd, ch.count, rp, &ch.recon_split);
@@ -662,8 +668,6 @@ extern "C" void ggemm_destroy(ggemm_handle_t h) {
   if (h->cublas) cublasDestroy(h->cublas);
   cudaFree(h->cublas_ws);
   cudaFree(h->pool);
-  cudaFree(h->wsA);
-  cudaFree(h->wsB);
   cudaFree(h->counters);
   delete h;
 }
@@ -737,11 +741,7 @@ extern "C" int ggemm_create_ex(ggemm_handle_t* out, int max_problems, size_t max
     want = std::min(want, frac * (double)total_b);
   }
   h->pool_cap = align_up(std::max<size_t>((size_t)want, 1 << 18), kAlign);
-  h->wsA_cap = 4 * max_A + P * 64 + 64;
-  h->wsB_cap = 4 * max_B + P * 64 + 64;
   CUA(cudaMalloc(&h->pool, h->pool_cap));
-  CUA(cudaMalloc(&h->wsA, h->wsA_cap * sizeof(int32_t)));
-  CUA(cudaMalloc(&h->wsB, h->wsB_cap * sizeof(int32_t)));
   CUA(cudaMalloc(&h->counters, sizeof(DevCounters)));
   CUA(cudaMemsetAsync(h->counters, 0, sizeof(DevCounters), stream));
 
@@ -764,7 +764,11 @@ extern "C" int ggemm_create_ex(ggemm_handle_t* out, int max_problems, size_t max
     for (auto* v : {&h->emu, &h->nat, &h->order, &h->ua_of, &h->ub_of, &h->ua_rep, &h->ub_rep,
                     &h->ua_n, &h->ub_n, &h->ua_chunk, &h->ub_chunk})
       v->resize(P);
-    for (auto* v : {&h->ua_img, &h->ub_img, &h->ua_ws, &h->ub_ws, &h->c32_off}) v->resize(P);
+    for (auto* v : {&h->ua_img, &h->ub_img, &h->ua_ws, &h->ub_ws, &h->c32_off, &h->pa_img,
+                    &h->pb_img, &h->pa_ws, &h->pb_ws})
+      v->resize(P);
+    h->pa_new.resize(P);
+    h->pb_new.resize(P);
     h->chunks.reserve(P + 1);
     h->ngroups.reserve(P);
     if (h->reuse.reserve(max_problems) != 0) FAIL(GGEMM_ERR_INVALID);

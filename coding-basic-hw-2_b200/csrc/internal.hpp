@@ -47,6 +47,7 @@ struct Chunk {
   size_t off_prep, off_prep_prefix, off_jobs, off_job_prefix, off_recon, off_recon_prefix;
   int num_prep, prep_blocks;
   size_t base_b, base_c;   // byte offsets of the chunk's B images and products in the pool
+  size_t base_wa, base_wb; // ... of its row (A) and column (B) workspace
   PrepSplit prep_split;    // descriptors sorted by prep instance (launch_prep)
   ReconSplit recon_split;  // ... by reconstruct instance (launch_recon)
   bool qscale;  // A images q-scaled (every problem of the chunk in the digit layout)
@@ -71,10 +72,6 @@ struct ggemm_handle_s {
   // the products (Chunk::base_b / base_c), so the split follows each call's shapes.
   int8_t* pool = nullptr;
   size_t pool_cap = 0;  // bytes
-  int32_t* wsA = nullptr;
-  size_t wsA_cap = 0;
-  int32_t* wsB = nullptr;
-  size_t wsB_cap = 0;
   g2::DevCounters* counters = nullptr;
 
   // one pinned host descriptor blob per slot, mirrored by one device blob per slot
@@ -90,8 +87,12 @@ struct ggemm_handle_s {
   std::vector<int> emu, nat, order;
   std::vector<int> ua_of, ub_of;          // per emulated problem: unique operand ids
   std::vector<int> ua_rep, ub_rep, ua_n, ub_n;
-  std::vector<int> ua_chunk, ub_chunk;    // last chunk that prepped a unique operand
-  std::vector<size_t> ua_img, ub_img, ua_ws, ub_ws;
+  std::vector<int> ua_chunk, ub_chunk;    // last chunk that placed a unique operand
+  std::vector<size_t> ua_img, ub_img, ua_ws, ub_ws;  // ... and where (while chunking)
+  // per emulated problem, in its own chunk: image / workspace offsets of its A and B, whether it
+  // prepares them there, and the offset of its products
+  std::vector<size_t> pa_img, pb_img, pa_ws, pb_ws;
+  std::vector<char> pa_new, pb_new;
   std::vector<size_t> c32_off;
   std::vector<g2::Chunk> chunks;
   g2::NativeGroups ngroups;

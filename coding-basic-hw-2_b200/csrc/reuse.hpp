@@ -3,8 +3,9 @@
 // src/operand_reuse.cpp:47-141):
 //   A key = (A pointer, lda, m, k), B key = (B pointer, ldb, n, k); under EXACT_N the moduli
 //   count is part of the key.  Unique operands are numbered in order of first appearance.
-//   PROMOTE links problems through shared operands (union-find) and runs every problem of a
-//   component with the component's largest N (the prep shift depends on N through T_N).
+//   PROMOTE treats problems that share an operand as connected and runs every problem of a
+//   connected component with the component's largest N (the prep shift depends on N through
+//   T_N).  The implementation (reuse.cpp) sorts keys and walks components breadth-first.
 #pragma once
 #include <cstdint>
 #include <vector>
@@ -35,11 +36,9 @@ class ReuseArena {
 
  private:
   int cap_ = 0;
-  uint32_t mask_ = 0, gen_ = 0;
-  std::vector<uint32_t> a_stamp_, b_stamp_;
-  std::vector<int> a_slot_, b_slot_;
   std::vector<int> ua_rep_, ua_nmod_, ub_rep_, ub_nmod_, prob_a_, prob_b_, eff_;
-  std::vector<int> parent_, cmax_;
+  std::vector<int> emu_, order_, run_first_, key_n_;     // per problem
+  std::vector<int> offs_, edges_, comp_, queue_, cmax_;  // operand graph (PROMOTE)
 };
 
 }  // namespace g2

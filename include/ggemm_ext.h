@@ -51,9 +51,10 @@ int ggemm_shard_group(const ggemm_problem_t* problems, int num, int num_shards,
  * Nothing is allocated: no cudaMalloc / cudaFree, no allocating library routine.
  *   num_moduli: 0 = adaptive (target 1e-15) or a fixed N in [2, 20];
  *   repair_mode: GGEMM_REPAIR_* (default = COUNT, as GGEMM_PATH_EMU_GROUPED).
- * Results equal ggemm_grouped_dgemm(GGEMM_PATH_EMU_GROUPED) of the same problem, bit for bit:
- * for alpha == 0 or k == 0 both compute C = beta C (C = 0, C not read, when beta == 0), which
- * the grouped call does through its native route.
+ * For alpha != 0 and k > 0, results equal ggemm_grouped_dgemm(GGEMM_PATH_EMU_GROUPED) of the
+ * same problem, bit for bit.  For alpha == 0 or k == 0 this computes C = beta C in its own kernel
+ * without reading A or B (C = +0, C not read, when beta == 0); the grouped call sends those
+ * problems to cuBLAS, which gives the same values but may give zeros of the other sign.
  * A problem whose scratch exceeds 64 MiB (about 1130^3 at N = 15) returns GGEMM_ERR_WORKSPACE
  * with a one-line message on stderr, before anything is enqueued; k > 131040 returns
  * GGEMM_ERR_UNSAFE.

@@ -201,7 +201,8 @@ def test_c4_full_size_emu_grouped_repair_on_vs_reference(g2, ref, cuda):
 def test_c4_full_size_auto_against_cublas_fp64(g2, cuda):
     """AUTO (repair ON) on the full C4 group: every finite entry within 2 gamma_{k+2} den of
     cuBLAS FP64 (both lie within gamma_{k+2} den of the exact value), non-finite entries of the
-    same class (NaN / +Inf / -Inf) as cuBLAS, alpha = 0 problems exactly beta C."""
+    same class (NaN / +Inf / -Inf) as cuBLAS, alpha = 0 problems (routed to cuBLAS) identical
+    to the native call."""
     wl = W.c4()
     grp = group(g2, wl)
     rc, st, C = run_ours(g2, grp, g2.PATH_AUTO, cfg_of(g2, wl), wl.min_k)
@@ -212,8 +213,10 @@ def test_c4_full_size_auto_against_cublas_fp64(g2, cuda):
         got = C[grp.c_off[i]:grp.c_off[i] + m * n]
         want = native[grp.c_off[i]:grp.c_off[i] + m * n]
         if it.alpha == 0.0:
-            c0 = grp.c0[grp.c_off[i]:grp.c_off[i] + m * n]
-            assert torch.equal(got, it.beta * c0), f"alpha=0 problem {i}"
+            # alpha = 0 goes to cuBLAS, as in the reference (src/planner.cpp:307-308); its
+            # grouped DGEMM still forms A B, so NaN / Inf in A reach C: same bytes as the
+            # native path
+            assert torch.equal(got.view(torch.int64), want.view(torch.int64)), f"alpha=0, {i}"
             continue
         a = grp.A[grp.a_off[it.a]:grp.a_off[it.a] + m * k].view(k, m).t()
         b = grp.B[grp.b_off[it.b]:grp.b_off[it.b] + k * n].view(n, k).t()

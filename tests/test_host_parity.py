@@ -120,6 +120,26 @@ def test_reuse_matches_reference(g2, ref, policy, seed):
     assert o1 == o2
 
 
+@pytest.mark.parametrize("policy", [0, 1])
+@pytest.mark.parametrize("seed", [21, 22, 23, 24])
+def test_reuse_matches_reference_sparse_chains(g2, ref, policy, seed):
+    """Many operands, sparse sharing (long promotion chains A - B - A ...), one pointer under
+    several (ld, rows, k) keys, and problems that are not emulated (nmod 0)."""
+    rng = np.random.default_rng(seed)
+    specs, nmod = [], []
+    for g in range(400):
+        a, b = int(rng.integers(0, 60)), int(rng.integers(0, 60))
+        k = [64, 96][int(rng.integers(0, 2))]
+        m = 40 + (a % 5)
+        lda = m + int(rng.integers(0, 2))
+        spec = list(_spec(m, 30 + b % 7, k, 1.0, 0.0, A=0x10000 * (a + 1), B=0x1000000 * (b + 1)))
+        spec[4] = lda
+        specs.append(tuple(spec))
+        nmod.append(int(rng.choice([0, 8, 14, 15, 16, 20])))
+    o1, o2 = _reuse_both(g2, ref, specs, nmod, policy)
+    assert o1 == o2
+
+
 def test_reuse_c5_pattern(g2, ref):
     """Config 5 shape: 16 shared A, 32 distinct B each -> 16 unique A, 512 unique B."""
     specs = [_spec(4096, 1024, 4096, 1.0, 1.0, A=0x1000 * (1 + g // 32), B=0x100000 * (g + 1))
