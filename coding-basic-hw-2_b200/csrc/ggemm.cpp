@@ -393,6 +393,26 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         if (ta != tb) return ta > tb;
         return a < b;
       });
+    // the paired GEMM (256 x 256 tiles on CTA pairs) when its row padding costs little
+    ch.pair = false;
+    if (!loop && !lbat && h->gemm_pair != 0) {
+      if (h->gemm_pair == 1) {
+        ch.pair = true;
+      } else {
+        int* mm = h->pair_m.data();
+        int* nn = h->pair_n.data();
+        int* kk = h->pair_k.data();
+        int* pl = h->pair_p.data();
+        for (int x = 0; x < ch.count; ++x) {
+          const ggemm_problem_t& p = probs[emu[ch.first + x]];
+          mm[x] = p.m;
+          nn[x] = p.n;
+          kk[x] = (p.k + 31) / 32;
+          pl[x] = plan[emu[ch.first + x]].num_moduli + 1;
+        }
+        ch.pair = gemm_pair_pays(mm, nn, kk, pl, ch.count, h->num_sms);
+      }
+    }
     long long tiles = 0;
     int jq = 0;
     for (int x = 0; x < ch.count; ++x) {
@@ -414,7 +434,8 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
       base.m = p.m;
       base.n = p.n;
       base.ksteps = (p.k + 31) / 32;
-      set_gemm_tiling(base);
+      if (ch.pair) set_gemm_tiling_pair(base);
+      else set_gemm_tiling(base);
       if (loop) {
         for (int l = 0; l <= N; ++l) {
           GemmJob jb = base;
@@ -550,7 +571,9 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
         ++*launches;
       }
     } else if (ch.tiles > 0) {
-      if (launch_gemm(jobs, jp, ch.count, ch.tiles, h->counters, s)) return GGEMM_ERR_I8GEMM;
+      const int e = ch.pair ? launch_gemm_pair(jobs, jp, ch.count, ch.tiles, h->counters, s)
+                            : launch_gemm(jobs, jp, ch.count, ch.tiles, h->counters, s);
+      if (e) return GGEMM_ERR_I8GEMM;
       ++*launches;
     }
     if (!mark(2)) return GGEMM_ERR_CUDA;
@@ -768,6 +791,7 @@ extern "C" int ggemm_create_ex(ggemm_handle_t* out, int max_problems, size_t max
                     &h->pb_img, &h->pa_ws, &h->pb_ws})
       v->resize(P);
     h->pa_new.resize(P);
+    for (auto* v : {&h->pair_m, &h->pair_n, &h->pair_k, &h->pair_p}) v->resize(P);
     h->pb_new.resize(P);
     h->chunks.reserve(P + 1);
     h->ngroups.reserve(P);
@@ -777,6 +801,10 @@ extern "C" int ggemm_create_ex(ggemm_handle_t* out, int max_problems, size_t max
   }
   if (const char* e = std::getenv("GGEMM_REUSE_PROMOTE")) h->reuse_promote = std::atoi(e) == 1;
   if (const char* e = std::getenv("GGEMM_STATS_REPAIR")) h->stats_repair = std::atoi(e) == 1;
+  if (const char* e = std::getenv("GGEMM_GEMM_PAIR")) {
+    const int v = std::atoi(e);
+    h->gemm_pair = (v == 0 || v == 1) ? v : -1;
+  }
   if (cudaStreamSynchronize(stream) != cudaSuccess) FAIL(GGEMM_ERR_CUDA);
 #undef CUA
 #undef FAIL

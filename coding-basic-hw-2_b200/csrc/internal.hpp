@@ -51,6 +51,7 @@ struct Chunk {
   PrepSplit prep_split;    // descriptors sorted by prep instance (launch_prep)
   ReconSplit recon_split;  // ... by reconstruct instance (launch_recon)
   bool qscale;  // A images q-scaled (every problem of the chunk in the digit layout)
+  bool pair;    // residue GEMM on CTA pairs (launch_gemm_pair)
   long long tiles, recon_blocks;
 };
 
@@ -94,6 +95,7 @@ struct ggemm_handle_s {
   std::vector<size_t> pa_img, pb_img, pa_ws, pb_ws;
   std::vector<char> pa_new, pb_new;
   std::vector<size_t> c32_off;
+  std::vector<int> pair_m, pair_n, pair_k, pair_p;  // gemm_pair_pays arguments of a chunk
   std::vector<g2::Chunk> chunks;
   g2::NativeGroups ngroups;
   std::vector<const void*> nat_ptrs;
@@ -102,6 +104,7 @@ struct ggemm_handle_s {
   g2::ReuseArena reuse;
   double rho_budget = 16.0;
   int reuse_promote = 0;
+  int gemm_pair = -1;  // GGEMM_GEMM_PAIR: -1 chosen per chunk (gemm_pair_pays), 0 never, 1 always
   int stats_repair = 0;
   int ws_diag_printed = 0;
   cudaEvent_t stage_ev[4] = {nullptr, nullptr, nullptr, nullptr};

@@ -831,6 +831,26 @@ __device__ __forceinline__ TileWalk tile_walk(long long T) {
   return w;
 }
 
+// Coordinates of a job's local tile: plane-major; inside a plane, bands of kBandRows rows of
+// row tiles (2048 operand rows), each walked column tile after column tile with the row tile
+// fastest.  The CTAs that run at the same time then share a band's A row panels and its
+// column tiles' B panels in L2 (row tile fastest over a whole plane made them share B but spread
+// over all of A: about ten times the operand bytes read from DRAM, measured).
+constexpr int kBandRows = 2048;
+__device__ __forceinline__ void job_tile(int local, const GemmJob& jb, int& plane, int& tm,
+                                         int& tn) {
+  const int tmc = jb.tm, tnc = jb.tn;
+  const int band = max(1, kBandRows / jb.bm);
+  const int per_plane = tmc * tnc;
+  plane = local / per_plane;
+  const int rem = local - plane * per_plane;
+  const int g = rem / (band * tnc);
+  const int within = rem - g * band * tnc;
+  const int rows = min(band, tmc - g * band);
+  tn = within / rows;
+  tm = g * band + (within - tn * rows);
+}
+
 // Tile t of the call: its job (warp-parallel owner search, so call by all 32 lanes), plane and
 // tile coordinates (a job has fewer than 2^31 tiles).
 __device__ __forceinline__ TileInfo decode_tile(const GemmJob* __restrict__ jobs,
@@ -839,13 +859,38 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmJob* __restrict__ jobs
   TileInfo ti;
   const int j = find_owner_warp(prefix, num, t);
   ti.job = jobs + j;
-  const int local = (int)(t - prefix[j]);
-  const int tm = ti.job->tm;
-  const int per_plane = tm * ti.job->tn;
-  ti.plane = local / per_plane;
-  const int rem = local - ti.plane * per_plane;
-  ti.tn = rem / tm;
-  ti.tm = rem - ti.tn * tm;
+  job_tile((int)(t - prefix[j]), *ti.job, ti.plane, ti.tm, ti.tn);
+  return ti;
+}
+
+// Builds a CTA's tile schedule {job, plane, tm, tn} in shared memory (sched), staging the job
+// prefix in `staged` (the still unused operand ring); whole block.
+__device__ __forceinline__ void build_schedule(const GemmJob* __restrict__ jobs,
+                                               const long long* __restrict__ prefix, int num,
+                                               const TileWalk& walk, long long* staged,
+                                               int4* sched) {
+  for (int x = threadIdx.x; x < num; x += blockDim.x) staged[x] = prefix[x];
+  __syncthreads();
+  for (int x = threadIdx.x; x < (int)walk.count(); x += blockDim.x) {
+    const long long t = walk.at(x);
+    int lo = 0, hi = num - 1;  // largest j with staged[j] <= t
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (staged[mid] <= t) lo = mid;
+      else hi = mid - 1;
+    }
+    int plane, tm, tn;
+    job_tile((int)(t - staged[lo]), jobs[lo], plane, tm, tn);
+    sched[x] = make_int4(lo, plane, tm, tn);
+  }
+  __syncthreads();  // the staged prefix in the operand ring is no longer read
+}
+__device__ __forceinline__ TileInfo sched_tile(const GemmJob* jobs, int4 r) {
+  TileInfo ti;
+  ti.job = jobs + r.x;
+  ti.plane = r.y;
+  ti.tm = r.z;
+  ti.tn = r.w;
   return ti;
 }
 
@@ -966,6 +1011,35 @@ __device__ __forceinline__ void gemm_digit_records(const GemmJob& jb, const Tile
   }
 }
 
+// Epilogue of one tile for one thread: TMEM lane = row of the tile at taddr (columns from 0),
+// products written in the job's layout (digits: gemm_digit_records; int32: column-major planes).
+__device__ __forceinline__ void gemm_tile_epilogue(const GemmJob& jb, const TileInfo& ti, int row,
+                                                   uint32_t taddr) {
+  // record columns of this tile that lie inside the problem
+  const int nch = min(jb.bn, jb.n - ti.tn * jb.bn + 31) / 32;
+  if (jb.y8 == 2) {
+    gemm_digit_records<true>(jb, ti, row, taddr, nch);
+  } else if (jb.y8) {
+    gemm_digit_records<false>(jb, ti, row, taddr, nch);
+  } else {
+    int32_t* C = jb.C + (long long)ti.plane * jb.c_plane;
+#pragma unroll 1
+    for (int c = 0; c < nch; ++c) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
+      tmem_ld_wait(v);
+      const int col0 = ti.tn * jb.bn + c * 32;
+      if (row < jb.m) {
+        int32_t* cp = C + row + (long long)col0 * jb.m;
+        const int ncol = min(32, jb.n - col0);
+#pragma unroll
+        for (int x = 0; x < 32; ++x)
+          if (x < ncol) cp[(long long)x * jb.m] = (int32_t)v[x];
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const GemmJob* __restrict__ jobs, const long long* __restrict__ prefix, int num,
                 long long total_tiles, DevCounters* cnt) {
@@ -999,38 +1073,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int4* sched = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(ctl) +
                                         ((sizeof(GemmSmemCtl) + 63) & ~size_t(63)));
   const bool cached = walk.count() <= kSchedMax && num <= kSchedJobs;  // block-uniform
-  if (cached) {
-    long long* sp = reinterpret_cast<long long*>(smem);
-    for (int x = threadIdx.x; x < num; x += blockDim.x) sp[x] = prefix[x];
-    __syncthreads();
-    for (int x = threadIdx.x; x < (int)walk.count(); x += blockDim.x) {
-      const long long t = walk.at(x);
-      int lo = 0, hi = num - 1;  // largest j with sp[j] <= t
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (sp[mid] <= t) lo = mid;
-        else hi = mid - 1;
-      }
-      const int local = (int)(t - sp[lo]);
-      const int tm = jobs[lo].tm;
-      const int per_plane = tm * jobs[lo].tn;
-      const int plane = local / per_plane;
-      const int rem = local - plane * per_plane;
-      sched[x] = make_int4(lo, plane, rem - (rem / tm) * tm, rem / tm);
-    }
-    __syncthreads();  // the staged prefix in the operand ring is no longer read
-  }
+  if (cached) build_schedule(jobs, prefix, num, walk, reinterpret_cast<long long*>(smem), sched);
   // tile `it` of this CTA's walk (warp-collective when not cached)
   auto tile_of = [&](long long it) -> TileInfo {
-    if (cached) {
-      const int4 r = sched[it];
-      TileInfo ti;
-      ti.job = jobs + r.x;
-      ti.plane = r.y;
-      ti.tm = r.z;
-      ti.tn = r.w;
-      return ti;
-    }
+    if (cached) return sched_tile(jobs, sched[it]);
     return decode_tile(jobs, prefix, num, walk.at(it));
   };
 
@@ -1159,29 +1205,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const int row = ti.tm * kGemmBM + quad * 32 + lane;
       const uint32_t taddr = tmem + (uint32_t)(buf * kGemmBNMax) + ((uint32_t)(quad * 32) << 16);
-      // record columns of this tile that lie inside the problem
-      const int nch = min(jb.bn, jb.n - ti.tn * jb.bn + 31) / 32;
-      if (jb.y8 == 2) {
-        gemm_digit_records<true>(jb, ti, row, taddr, nch);
-      } else if (jb.y8) {
-        gemm_digit_records<false>(jb, ti, row, taddr, nch);
-      } else {
-        int32_t* C = jb.C + (long long)ti.plane * jb.c_plane;
-#pragma unroll 1
-        for (int c = 0; c < nch; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
-          tmem_ld_wait(v);
-          const int col0 = ti.tn * jb.bn + c * 32;
-          if (row < jb.m) {
-            int32_t* cp = C + row + (long long)col0 * jb.m;
-            const int ncol = min(32, jb.n - col0);
-#pragma unroll
-            for (int x = 0; x < 32; ++x)
-              if (x < ncol) cp[(long long)x * jb.m] = (int32_t)v[x];
-          }
-        }
-      }
+      gemm_tile_epilogue(jb, ti, row, taddr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->acc_empty[buf]);
@@ -1195,6 +1219,261 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ======================================================== paired residue GEMM (CTA pairs)
+// A cluster of two CTAs computes 256 x 256 tiles with tcgen05.mma.cta_group::2.  CTA r holds the
+// tile's A rows [128 r, 128 r + 128) and B rows (tile columns) [r W / 2, (r + 1) W / 2) of the
+// tile's MMA width W, in the same shared-memory image layout as gemm_kernel; one thread of CTA 0
+// issues the MMAs, and each CTA's TMEM receives its 128 rows x W columns.  Per SM and 32-byte K
+// step that is 4 KB of A and 4 KB of B copied into shared memory, against 4 + 8 KB for
+// gemm_kernel's 128 x 256 tile.
+// Each CTA's producer bulk-copies its own valid row groups into its own shared memory, counted
+// on its own stage barrier (the same data path as gemm_kernel; 2D tensor copies of this layout
+// measured 1.7x slower).  Warp 1 of CTA 1, idle otherwise, relays each of its stages that landed
+// to CTA 0 with one remote arrival on CTA 0's peer_full barrier; CTA 0's MMA thread waits on its
+// own full barrier and on peer_full.  MMA commits multicast to both CTAs' stage-free and
+// accumulator-full barriers; the epilogue warps of both CTAs arrive on CTA 0's accumulator-free
+// barrier.  No load uses cluster multicast.
+// Every wait is bounded (kWaitNs).  Copies in flight when a CTA gives up land within
+// microseconds, long before the partner's own bounded waits end and the CTAs pass the final
+// cluster barrier, so neither CTA exits while the other can still touch its shared memory.
+constexpr int kStages2 = 6;
+constexpr int kStepBytes2 = 16 * 256;                  // one K step of 128 rows
+constexpr int kStageBytes2 = kKS * 2 * kStepBytes2;    // kKS K steps of A and of B
+constexpr int kGemm2Rows = 256, kGemm2Cols = 256;
+struct GemmSmemCtl2 {
+  uint64_t full[kStages2], peer_full[kStages2], empty[kStages2], acc_full[2], acc_empty[2], drain;
+  uint32_t tmem_base;
+  int abort;
+};
+static_assert((kSchedJobs + 1) * 8 <= kStages2 * kStageBytes2, "prefix staging");
+constexpr size_t kGemm2Smem =
+    1024 + kStages2 * kStageBytes2 + sizeof(GemmSmemCtl2) + 64 + kSchedMax * sizeof(int4);
+
+__device__ __forceinline__ bool bounded_wait_pair(uint64_t* bar, uint32_t parity,
+                                                  GemmSmemCtl2* ctl, DevCounters* cnt) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t deadline = global_timer_ns() + kWaitNs;
+  if (mbar_wait(bar, parity, deadline, &ctl->abort)) return true;
+  ctl->abort = 1;
+  atomicCAS(&cnt->status, 0u, (unsigned)kStatusGemmTimeout);
+  return false;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const GemmJob* __restrict__ jobs, const long long* __restrict__ prefix,
+                     int num, long long total_tiles, DevCounters* cnt) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  GemmSmemCtl2* ctl = reinterpret_cast<GemmSmemCtl2*>(smem + kStages2 * kStageBytes2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(&ctl->full[s], 1);       // this CTA's producer arms it; its own copies complete it
+      mbar_init(&ctl->peer_full[s], 1);  // (CTA 0) CTA 1's relay, once CTA 1's stage landed
+      mbar_init(&ctl->empty[s], 1);      // one multicast commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->acc_full[b], 1);   // one multicast commit
+      mbar_init(&ctl->acc_empty[b], 8);  // 4 epilogue warps of each CTA (used in CTA 0)
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(&ctl->tmem_base, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  // the pair's walk: pair b of G pairs (both CTAs of a pair walk the same tiles)
+  TileWalk walk;
+  {
+    const long long T = total_tiles, mid = T / 2;
+    walk.T = T;
+    walk.b = (int)(blockIdx.x >> 1);
+    walk.G = (int)(gridDim.x >> 1);
+    walk.nf = mid > walk.b ? (mid - 1 - walk.b) / walk.G + 1 : 0;
+    walk.nb = T - 1 - walk.b >= mid ? (T - 1 - walk.b - mid) / walk.G + 1 : 0;
+  }
+  int4* sched = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(ctl) +
+                                        ((sizeof(GemmSmemCtl2) + 63) & ~size_t(63)));
+  const bool cached = walk.count() <= kSchedMax && num <= kSchedJobs;  // block-uniform
+  if (cached) build_schedule(jobs, prefix, num, walk, reinterpret_cast<long long*>(smem), sched);
+  auto tile_of = [&](long long it) -> TileInfo {
+    if (cached) return sched_tile(jobs, sched[it]);
+    return decode_tile(jobs, prefix, num, walk.at(it));
+  };
+  // MMA width of a tile: its columns inside the problem, rounded up to 32 (each CTA then holds
+  // a multiple of 16 B rows)
+  auto width_of = [](const GemmJob& jb, int tn) {
+    return min(kGemm2Cols, (jb.n - tn * kGemm2Cols + 31) & ~31);
+  };
+
+  if (warp == 0) {
+    // --------------------------------------------------------------------- producer
+    // valid row groups of this CTA: A rows [256 tm + 128 r, + 128), B rows (tile columns)
+    // [256 tn + r W / 2, + W / 2); groups past the image are not copied (their accumulator rows /
+    // columns are never stored)
+    int stage = 0;
+    uint32_t phase = 0;
+    for (long long it = 0;
+         it < walk.count() && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort); ++it) {
+      const TileInfo ti = tile_of(it);
+      const GemmJob& jb = *ti.job;
+      const int W = width_of(jb, ti.tn);
+      const int g0a = ti.tm * 32 + (int)rank * 16;
+      const int g0b = ti.tn * 32 + (int)rank * (W / 16);
+      const int ga = max(0, min(16, jb.rga - g0a));
+      const int gb = max(0, min(W / 16, jb.rgb - g0b));
+      const int8_t* A = jb.A + (long long)ti.plane * jb.a_plane + (long long)g0a * 256;
+      const int8_t* B = jb.B + (long long)ti.plane * jb.b_plane + (long long)g0b * 256;
+      const long long astep = (long long)jb.rga * 256, bstep = (long long)jb.rgb * 256;
+      bool ok = true;
+      for (int ks = 0; ks < jb.ksteps; ks += kKS) {
+        const int nst = min(kKS, jb.ksteps - ks);
+        if (lane == 0) {
+          ok = bounded_wait_pair(&ctl->empty[stage], phase ^ 1u, ctl, cnt);
+          if (ok) mbar_arrive_expect_tx(&ctl->full[stage], (uint32_t)(nst * (ga + gb) * 256));
+        }
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+        if (!ok) break;
+        uint8_t* sa = smem + stage * kStageBytes2;
+        uint8_t* sb = sa + kKS * kStepBytes2;
+        if (lane < nst) {
+          if (ga > 0)
+            bulk_g2s(sa + lane * kStepBytes2, A + (long long)(ks + lane) * astep,
+                     (uint32_t)(ga * 256), &ctl->full[stage]);
+        } else if (lane >= kKS && lane < kKS + nst) {
+          if (gb > 0)
+            bulk_g2s(sb + (lane - kKS) * kStepBytes2, B + (long long)(ks + lane - kKS) * bstep,
+                     (uint32_t)(gb * 256), &ctl->full[stage]);
+        }
+        __syncwarp();
+        if (++stage == kStages2) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 1 && rank == 0) {
+    // ------------------------------------------------------- MMA issuer (CTA 0, one lane)
+    int stage = 0;
+    uint32_t phase = 0;
+    int buf = 0;
+    uint32_t acc_phase = 0;
+    for (long long it = 0;
+         it < walk.count() && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort); ++it) {
+      const TileInfo ti = tile_of(it);
+      const int ksteps = ti.job->ksteps;
+      const uint32_t idesc = idesc_i8(kGemm2Rows, width_of(*ti.job, ti.tn));
+      bool ok = true;
+      if (lane == 0) {
+        ok = bounded_wait_pair(&ctl->acc_empty[buf], acc_phase ^ 1u, ctl, cnt);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t d_tmem = tmem + (uint32_t)(buf * kGemm2Cols);
+          for (int ks = 0; ks < ksteps; ks += kKS) {
+            const int nst = min(kKS, ksteps - ks);
+            if (!bounded_wait_pair(&ctl->full[stage], phase, ctl, cnt) ||
+                !bounded_wait_pair(&ctl->peer_full[stage], phase, ctl, cnt)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_addr(smem + stage * kStageBytes2);
+            const uint32_t sb = sa + kKS * kStepBytes2;
+            for (int j = 0; j < nst; ++j) {
+              const uint64_t ad = smem_desc_sw32(sa + j * kStepBytes2, 256);
+              const uint64_t bd = smem_desc_sw32(sb + j * kStepBytes2, 256);
+              mma_i8_pair(d_tmem, ad, bd, idesc, (ks > 0 || j > 0) ? 1u : 0u);
+            }
+            mma_commit_pair(&ctl->empty[stage], 3);
+            if (++stage == kStages2) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (ok) mma_commit_pair(&ctl->acc_full[buf], 3);
+        }
+      }
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+      if (++buf == 2) {
+        buf = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    // both CTAs' drain barriers complete once every MMA issued above has completed
+    if (lane == 0) mma_commit_pair(&ctl->drain, 3);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- relay (CTA 1, one lane)
+    int stage = 0;
+    uint32_t phase = 0;
+    for (long long it = 0;
+         it < walk.count() && !__any_sync(0xFFFFFFFFu, *(volatile int*)&ctl->abort); ++it) {
+      const int ksteps = tile_of(it).job->ksteps;
+      bool ok = true;
+      if (lane == 0) {
+        for (int ks = 0; ks < ksteps; ks += kKS) {
+          if (!bounded_wait_pair(&ctl->full[stage], phase, ctl, cnt)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_cluster(mapa_shared(smem_addr(&ctl->peer_full[stage]), 0));
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+    }
+  } else {
+    // ------------------------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    int buf = 0;
+    uint32_t acc_phase = 0;
+    for (long long it = 0; it < walk.count(); ++it) {
+      const TileInfo ti = tile_of(it);
+      const GemmJob& jb = *ti.job;
+      bool ok = true;
+      if (lane == 0) ok = bounded_wait_pair(&ctl->acc_full[buf], acc_phase, ctl, cnt);
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = ti.tm * kGemm2Rows + (int)rank * 128 + quad * 32 + lane;
+      const uint32_t taddr = tmem + (uint32_t)(buf * kGemm2Cols) + ((uint32_t)(quad * 32) << 16);
+      gemm_tile_epilogue(jb, ti, row, taddr);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&ctl->acc_empty[buf]), 0));
+      if (++buf == 2) {
+        buf = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+  // every MMA of the pair has completed before TMEM is released, and neither CTA exits before
+  // the other is done with the pair's barriers and shared memory
+  if (threadIdx.x == 0) {
+    int no_abort = 0;
+    mbar_wait(&ctl->drain, 0, global_timer_ns() + kWaitNs, &no_abort);
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc_pair(tmem, 512);
 }
 
 // ================================================================== bounded-wait probe
@@ -1690,7 +1969,9 @@ int upload_tables_current_device() {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   g_sms[dev] = sms > 0 ? sms : 148;
   if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)kGemmSmem) != cudaSuccess)
+                           (int)kGemmSmem) != cudaSuccess ||
+      cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kGemm2Smem) != cudaSuccess)
     return 3;
   if (cudaFuncSetAttribute(prep_kernel<false, 14>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kPrepSmem) != cudaSuccess ||
@@ -1747,6 +2028,15 @@ int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long 
   const long long grid = std::min<long long>(total_tiles, (long long)current_device_sms());
   gemm_kernel<<<(unsigned)grid, kGemmThreads, kGemmSmem, s>>>(d_jobs, d_prefix, num, total_tiles,
                                                               cnt);
+  return (int)cudaGetLastError();
+}
+
+int launch_gemm_pair(const GemmJob* d_jobs, const long long* d_prefix, int num,
+                     long long total_tiles, DevCounters* cnt, cudaStream_t s) {
+  if (num <= 0 || total_tiles <= 0) return 0;
+  const long long pairs = std::min<long long>(total_tiles, (long long)current_device_sms() / 2);
+  gemm_pair_kernel<<<(unsigned)(2 * pairs), kGemmThreads, kGemm2Smem, s>>>(d_jobs, d_prefix, num,
+                                                                          total_tiles, cnt);
   return (int)cudaGetLastError();
 }
 

@@ -54,7 +54,8 @@ struct GemmJob {
   long long a_plane, b_plane, c_plane, y_plane;
   int m, n, ksteps, planes;
   int rga, rgb, tm, tn;  // row groups of A / B, tile rows / columns
-  int bn;                // tile width: 256 columns, or 128 for n <= 128
+  int bm, bn;            // tile height (128, or 256 on CTA pairs) and width (256, or 128 for
+                         // n <= 128 on single CTAs)
   int N, plane0, y8;     // moduli, index of the job's first plane, output layout
 };
 
@@ -62,11 +63,36 @@ constexpr int kGemmBM = 128, kGemmBNMax = 256;
 
 // Tile shape of one problem: 128 rows x 256 columns (128 when n <= 128); requires m, n set.
 inline void set_gemm_tiling(GemmJob& j) {
+  j.bm = kGemmBM;
   j.bn = j.n > 128 ? 256 : 128;
   j.tm = (j.m + kGemmBM - 1) / kGemmBM;
   j.tn = (j.n + j.bn - 1) / j.bn;
   j.rga = (j.m + 7) / 8;
   j.rgb = (j.n + 7) / 8;
+}
+// Tile shape of the paired GEMM (launch_gemm_pair): 256 x 256 tiles (a CTA pair each).
+inline void set_gemm_tiling_pair(GemmJob& j) {
+  j.bm = 256;
+  j.bn = 256;
+  j.tm = (j.m + 255) / 256;
+  j.tn = (j.n + 255) / 256;
+  j.rga = (j.m + 7) / 8;
+  j.rgb = (j.n + 7) / 8;
+}
+// Whether a set of problems runs on the paired GEMM: its 256-row tiles pad the rows by at most
+// 10 % more multiply-adds than gemm_kernel's 128-row tiles, and there are tiles for every pair
+// of SMs.  m, n, ksteps, planes per problem.
+inline bool gemm_pair_pays(const int* m, const int* n, const int* ksteps, const int* planes,
+                           int num, int num_sms) {
+  double w1 = 0, w2 = 0;
+  long long tiles = 0;
+  for (int i = 0; i < num; ++i) {
+    const double per = (double)n[i] * ksteps[i] * planes[i];
+    w1 += (double)((m[i] + 127) / 128 * 128) * per;
+    w2 += (double)((m[i] + 255) / 256 * 256) * per;
+    tiles += (long long)((m[i] + 255) / 256) * ((n[i] + 255) / 256) * planes[i];
+  }
+  return w2 <= 1.1 * w1 && tiles >= num_sms;
 }
 constexpr int kPrepThreads = 256, kReconThreads = 256, kReconPerThread = 4;
 
@@ -137,6 +163,9 @@ int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, const Pre
                 DevCounters* cnt, cudaStream_t s, int* launches = nullptr);
 int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long long total_tiles,
                 DevCounters* cnt, cudaStream_t s);
+// The paired GEMM (CTA pairs, tcgen05.mma.cta_group::2) over jobs tiled by set_gemm_tiling_pair.
+int launch_gemm_pair(const GemmJob* d_jobs, const long long* d_prefix, int num,
+                     long long total_tiles, DevCounters* cnt, cudaStream_t s);
 // Reconstruct: compiled per repair mode and per class of moduli counts (N = 14, 15, 16 each, the
 // rest together); descriptors sorted by class, class c owning descriptors [first[c],
 // first[c + 1]) and blocks [block0[c], block0[c + 1]) (blocks per descriptor: recon_job_blocks).

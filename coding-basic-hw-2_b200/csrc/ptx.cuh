@@ -184,6 +184,66 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
                : "memory");
 }
 
+// ------------------------------------------------------------------ CTA pairs (clusters of 2)
+// The paired residue GEMM runs two CTAs per cluster: tcgen05.mma.cta_group::2 issued by CTA 0
+// computes a 256-row tile whose A rows are split between the two CTAs' shared memory (128 each)
+// and whose B rows (the tile's N) are split in halves, each CTA keeping its 128 accumulator rows
+// in its own TMEM.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of both CTAs: arrive (release) and wait (acquire) on the cluster barrier.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// The shared::cluster address of this CTA's shared address `saddr` mapped into CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier given by its shared::cluster address (possibly in the peer CTA).  The
+// arrivals this library makes there follow tcgen05.fence::before_thread_sync (TMEM reads done);
+// the tensor-core side orders through tcgen05.fence::after_thread_sync, so the default
+// semantics suffice (a cluster-scope release costs a fence per arrival).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_addr(dst_smem)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+// D[tmem of both CTAs] (+)= A[both CTAs' smem] * B[both CTAs' smem]^T (M = 256 split 128 / 128,
+// N split in halves), issued by one thread of CTA 0.
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier at the same shared offset in every CTA of `mask` when all
+// tcgen05.mma previously issued by this thread have completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_addr(bar)),
+      "h"(mask)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor (sm_100 layout): K-major operand, 32-byte swizzle.
 //   bits [0,14)  start address >> 4
 //   bits [16,30) leading byte offset >> 4 (ignored for swizzled K-major; 1 by convention)

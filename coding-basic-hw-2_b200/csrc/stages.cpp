@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -122,18 +124,38 @@ extern "C" int ggemm_stage_gemm(const ggemm_gemm_desc_t* descs, int num, void* s
         return GGEMM_ERR_INVALID;
     }
     jobs[i] = j;
+  }
+  // Paired GEMM (GGEMM_GEMM_PAIR: 1 always, 0 never, unset: when gemm_pair_pays).
+  const char* env = std::getenv("GGEMM_GEMM_PAIR");
+  const int force = env ? std::atoi(env) : -1;
+  std::vector<int> pm, pn, pk, pp;
+  for (int i = 0; i < num; ++i) {
+    const GemmJob& j = jobs[i];
+    if (j.planes <= 0) continue;
+    pm.push_back(j.m);
+    pn.push_back(j.n);
+    pk.push_back(j.ksteps);
+    pp.push_back(j.planes);
+  }
+  const bool pair = !pm.empty() && (force == 1 || (force != 0 &&
+                                                   gemm_pair_pays(pm.data(), pn.data(), pk.data(),
+                                                                  pp.data(), (int)pm.size(),
+                                                                  current_device_sms())));
+  for (int i = 0; i < num; ++i) {
+    if (pair) set_gemm_tiling_pair(jobs[i]);
     pre[i] = tiles;
-    tiles += gemm_tiles(j);
+    tiles += gemm_tiles(jobs[i]);
   }
   pre[num] = tiles;
   int r = copy_blob(scratch, scratch_bytes, bytes, s);
   if (r) return r;
   const char* db = static_cast<const char*>(scratch);
-  return launch_gemm(reinterpret_cast<const GemmJob*>(db),
-                     reinterpret_cast<const long long*>(db + off_p), num, tiles,
-                     static_cast<DevCounters*>(counters), s)
-             ? GGEMM_ERR_I8GEMM
-             : GGEMM_OK;
+  const GemmJob* dj = reinterpret_cast<const GemmJob*>(db);
+  const long long* dp = reinterpret_cast<const long long*>(db + off_p);
+  DevCounters* cnt = static_cast<DevCounters*>(counters);
+  const int e = pair ? launch_gemm_pair(dj, dp, num, tiles, cnt, s)
+                     : launch_gemm(dj, dp, num, tiles, cnt, s);
+  return e ? GGEMM_ERR_I8GEMM : GGEMM_OK;
 }
 
 extern "C" int ggemm_stage_recon(const ggemm_recon_desc_t* descs, int num, int repair_mode,

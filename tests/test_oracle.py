@@ -51,7 +51,8 @@ def test_tables_exact_integers(oracle):
 
 
 def test_published_constants(oracle):
-    """SURVEY Appendix A values (reference host code): log2 P, log2 u1, T, bounds."""
+    """Values of the reference host code (src/moduli.h:124-181, src/ozaki2_numerics.cu:639-673,
+    re-derived from its sources): log2 P, log2 u1, T, bounds."""
     t = _tables(oracle.tables_bytes())
     rows = {
         8: (63.50, 7, 2.5551e9, 2.505e-8, 1.002e-7, 1.417e-7),
@@ -71,7 +72,7 @@ def test_published_constants(oracle):
 
 
 def test_choose_tables(oracle):
-    """results/numerics_perf_511101.log and SURVEY Appendix A."""
+    """The published choose table, results/numerics_perf_511101.log:1-15."""
     got = {k: oracle.choose(k, 1e-15) for k in (256, 1024, 4096, 16384, 65536, 131072)}
     assert got == {256: 15, 1024: 15, 4096: 15, 16384: 16, 65536: 16, 131072: -1}
     assert oracle.choose(16, 1e-15) == 14
