@@ -460,6 +460,7 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
     }
     if (!loop) jp[jq] = tiles;
     ch.tiles = tiles;
+    ch.ragged = gemm_jobs_ragged(jobs, jq);
     for (int x = 0; x < ch.count; ++x) {
       const int j = ch.first + x;
       const int g = emu[j];
@@ -567,12 +568,14 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
       set_gemm_tiling(shape);
       const long long tiles = (long long)shape.tm * shape.tn;
       for (int q = 0; q < planes && tiles > 0; ++q) {
-        if (launch_gemm(jobs + q, jp + 2 * q, 1, tiles, h->counters, s)) return GGEMM_ERR_I8GEMM;
+        if (launch_gemm(jobs + q, jp + 2 * q, 1, tiles, h->counters, s, false))
+          return GGEMM_ERR_I8GEMM;
         ++*launches;
       }
     } else if (ch.tiles > 0) {
-      const int e = ch.pair ? launch_gemm_pair(jobs, jp, ch.count, ch.tiles, h->counters, s)
-                            : launch_gemm(jobs, jp, ch.count, ch.tiles, h->counters, s);
+      const int e =
+          ch.pair ? launch_gemm_pair(jobs, jp, ch.count, ch.tiles, h->counters, s, ch.ragged)
+                  : launch_gemm(jobs, jp, ch.count, ch.tiles, h->counters, s, ch.ragged);
       if (e) return GGEMM_ERR_I8GEMM;
       ++*launches;
     }

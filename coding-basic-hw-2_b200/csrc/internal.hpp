@@ -52,6 +52,7 @@ struct Chunk {
   ReconSplit recon_split;  // ... by reconstruct instance (launch_recon)
   bool qscale;  // A images q-scaled (every problem of the chunk in the digit layout)
   bool pair;    // residue GEMM on CTA pairs (launch_gemm_pair)
+  bool ragged;  // jobs of different K depth (two-ended tile walk)
   long long tiles, recon_blocks;
 };
 

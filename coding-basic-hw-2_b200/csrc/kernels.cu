@@ -764,7 +764,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
 // Two TMEM accumulators (2 x 256 columns, all of TMEM) let the epilogue of one tile overlap the
 // MMAs of the next.  The 256-column tile halves the operand bytes fetched per MAC of the
 // B side, which (with 128 x 128 tiles) bound the kernel by L2 -> SM traffic.  Tiles come from a
-// host-side LPT order; each CTA walks it from both ends (TileWalk) and keeps its walk's tile
+// host-side LPT order; each CTA walks it from both ends when the jobs differ in depth (TileWalk)
+// and keeps its walk's tile
 // coordinates in shared memory (the schedule below).
 constexpr int kKS = 4;     // 32-byte K steps per pipeline stage
 constexpr int kStages = 4;  // kStages * kKS * 12 KB of operands in flight
@@ -820,12 +821,15 @@ struct TileWalk {
   }
 };
 
-__device__ __forceinline__ TileWalk tile_walk(long long T) {
+// Walk b of G over T tiles.  both_ends: alternate between the heavy front and the light back
+// (groups whose jobs differ in depth); otherwise the front walk covers every tile in order, so
+// the tiles in flight at any time are consecutive (one band: shared operand panels in L2).
+__device__ __forceinline__ TileWalk tile_walk(long long T, int b, int G, bool both_ends) {
   TileWalk w;
   w.T = T;
-  w.b = (int)blockIdx.x;
-  w.G = (int)gridDim.x;
-  const long long mid = T / 2;
+  w.b = b;
+  w.G = G;
+  const long long mid = both_ends ? T / 2 : T;
   w.nf = mid > w.b ? (mid - 1 - w.b) / w.G + 1 : 0;
   w.nb = T - 1 - w.b >= mid ? (T - 1 - w.b - mid) / w.G + 1 : 0;
   return w;
@@ -1042,7 +1046,7 @@ __device__ __forceinline__ void gemm_tile_epilogue(const GemmJob& jb, const Tile
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const GemmJob* __restrict__ jobs, const long long* __restrict__ prefix, int num,
-                long long total_tiles, DevCounters* cnt) {
+                long long total_tiles, DevCounters* cnt, int both_ends) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   GemmSmemCtl* ctl = reinterpret_cast<GemmSmemCtl*>(smem + kStages * kStageBytes);
@@ -1069,7 +1073,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  const TileWalk walk = tile_walk(total_tiles);
+  const TileWalk walk = tile_walk(total_tiles, (int)blockIdx.x, (int)gridDim.x, both_ends != 0);
   int4* sched = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(ctl) +
                                         ((sizeof(GemmSmemCtl) + 63) & ~size_t(63)));
   const bool cached = walk.count() <= kSchedMax && num <= kSchedJobs;  // block-uniform
@@ -1263,7 +1267,7 @@ __device__ __forceinline__ bool bounded_wait_pair(uint64_t* bar, uint32_t parity
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_pair_kernel(const GemmJob* __restrict__ jobs, const long long* __restrict__ prefix,
-                     int num, long long total_tiles, DevCounters* cnt) {
+                     int num, long long total_tiles, DevCounters* cnt, int both_ends) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   GemmSmemCtl2* ctl = reinterpret_cast<GemmSmemCtl2*>(smem + kStages2 * kStageBytes2);
@@ -1294,15 +1298,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
   // the pair's walk: pair b of G pairs (both CTAs of a pair walk the same tiles)
-  TileWalk walk;
-  {
-    const long long T = total_tiles, mid = T / 2;
-    walk.T = T;
-    walk.b = (int)(blockIdx.x >> 1);
-    walk.G = (int)(gridDim.x >> 1);
-    walk.nf = mid > walk.b ? (mid - 1 - walk.b) / walk.G + 1 : 0;
-    walk.nb = T - 1 - walk.b >= mid ? (T - 1 - walk.b - mid) / walk.G + 1 : 0;
-  }
+  const TileWalk walk =
+      tile_walk(total_tiles, (int)(blockIdx.x >> 1), (int)(gridDim.x >> 1), both_ends != 0);
   int4* sched = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(ctl) +
                                         ((sizeof(GemmSmemCtl2) + 63) & ~size_t(63)));
   const bool cached = walk.count() <= kSchedMax && num <= kSchedJobs;  // block-uniform
@@ -2023,20 +2020,20 @@ int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, const Pre
 }
 
 int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long long total_tiles,
-                DevCounters* cnt, cudaStream_t s) {
+                DevCounters* cnt, cudaStream_t s, bool both_ends) {
   if (num <= 0 || total_tiles <= 0) return 0;
   const long long grid = std::min<long long>(total_tiles, (long long)current_device_sms());
   gemm_kernel<<<(unsigned)grid, kGemmThreads, kGemmSmem, s>>>(d_jobs, d_prefix, num, total_tiles,
-                                                              cnt);
+                                                              cnt, both_ends ? 1 : 0);
   return (int)cudaGetLastError();
 }
 
 int launch_gemm_pair(const GemmJob* d_jobs, const long long* d_prefix, int num,
-                     long long total_tiles, DevCounters* cnt, cudaStream_t s) {
+                     long long total_tiles, DevCounters* cnt, cudaStream_t s, bool both_ends) {
   if (num <= 0 || total_tiles <= 0) return 0;
   const long long pairs = std::min<long long>(total_tiles, (long long)current_device_sms() / 2);
-  gemm_pair_kernel<<<(unsigned)(2 * pairs), kGemmThreads, kGemm2Smem, s>>>(d_jobs, d_prefix, num,
-                                                                          total_tiles, cnt);
+  gemm_pair_kernel<<<(unsigned)(2 * pairs), kGemmThreads, kGemm2Smem, s>>>(
+      d_jobs, d_prefix, num, total_tiles, cnt, both_ends ? 1 : 0);
   return (int)cudaGetLastError();
 }
 
