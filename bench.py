@@ -174,8 +174,8 @@ def moduli_of(g2, grp, cfg, path):
     route = (ctypes.c_int * max(1, num))()
     nmod = (ctypes.c_int * max(1, num))()
     tile = (ctypes.c_int * max(1, num))()
-    rc = g2.lib.ggemm_stage_plan(grp.problems, num, ctypes.byref(cfg), path, 148, 36e12, 2.5e15,
-                                 6.0e12, 32.0 ** 3, 16.0, route, nmod, tile)
+    rc = g2.lib.ggemm_stage_plan(grp.problems, num, ctypes.byref(cfg), path, 148, 0.0, 0.0, 0.0,
+                                 -1.0, 0.0, route, nmod, tile)  # the library's own model
     if rc != 0:
         raise RuntimeError(f"ggemm_stage_plan rc={rc}")
     return [nmod[i] if route[i] == 0 else 0 for i in range(num)]

@@ -737,7 +737,7 @@ extern "C" int ggemm_create_ex(ggemm_handle_t* out, int max_problems, size_t max
       cudaGetDeviceProperties(&prop, h->device) != cudaSuccess)
     FAIL(GGEMM_ERR_CUDA);
   h->num_sms = prop.multiProcessorCount;
-  device_model_init(&h->dm, prop.major, h->num_sms);
+  device_model_init(&h->dm, h->num_sms);
   h->rho_budget = env_rho_budget();
   if (upload_tables_current_device() != 0) FAIL(GGEMM_ERR_NUMERICS);
 

@@ -1,100 +1,117 @@
 // planner.cpp -- see planner.hpp.  Host only; no allocation.
 #include "planner.hpp"
 
+#include <dlfcn.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <string>
 
 #include "crt.hpp"
 
 namespace g2 {
 namespace {
 
-inline double kp_of(int k) { return (double)(((size_t)k + 31) / 32 * 32); }
-inline double tile_dim(int cfg) { return cfg == 0 ? 128.0 : (cfg == 1 ? 64.0 : 32.0); }
-inline double round_up(double x, double t) { return std::ceil(x / t) * t; }
-inline double tiles_of(int m, int n, int cfg) {
-  const double t = tile_dim(cfg);
-  return std::ceil(m / t) * std::ceil(n / t);
+// Built-in B200 constants: calib/b200.json as fitted on this pool's B200s (used when no file is
+// found next to the library).
+constexpr DeviceModel kB200Default = {
+    148,
+    /*prep_bw=*/2.157e+12, /*prep_block_s=*/2.908e-06,
+    /*gemm_ops=*/2.376e+15, /*gemm_tile_s=*/1.57e-06,
+    /*recon_bw=*/8.09e+12, /*recon_block_s=*/2.904e-06,
+    /*fp64_flops=*/3.13e+13, /*native_problem_s=*/1.066e-07,
+    /*tiny_mnk=*/32.0 * 32.0 * 32.0, 0};
+
+bool json_number(const char* txt, const char* key, double* v) {
+  char pat[96];
+  std::snprintf(pat, sizeof pat, "\"%s\"", key);
+  const char* p = std::strstr(txt, pat);
+  if (!p) return false;
+  p = std::strchr(p + std::strlen(pat), ':');
+  if (!p) return false;
+  char* end = nullptr;
+  const double x = std::strtod(p + 1, &end);
+  if (end == p + 1 || !(x >= 0)) return false;
+  *v = x;
+  return true;
 }
 
-// Cost-model tile classes, their relative INT8 efficiency, resident tiles per SM and the
-// number of FP64 read passes of prep (reference src/planner.cpp:151-172).
-constexpr int kTileCfgs = 3;
-constexpr double kTileEff[kTileCfgs] = {1.0, 0.63, 0.30};
-constexpr double kSlotsPerSm = 2.0;
-constexpr double kPrepPasses = 2.0;
-constexpr double kWsIntsPerRow = 4.0;
+double env_double(const char* name, double lo, double hi, bool* used) {
+  const char* s = std::getenv(name);
+  if (!s || !*s) return 0;
+  char* end = nullptr;
+  const double v = std::strtod(s, &end);
+  if (end == s || !(v >= lo && v <= hi)) {
+    std::fprintf(stderr, "[ggemm] WARNING: %s=%s outside [%g, %g], ignored\n", name, s, lo, hi);
+    return 0;
+  }
+  *used = true;
+  return v;
+}
 
-// Largest tile whose padded-area efficiency is >= 0.75, else the most efficient one.
-int tile_by_padding(int m, int n) {
-  int best = kTileCfgs - 1;
-  double best_eff = -1;
-  for (int c = 0; c < kTileCfgs; ++c) {
-    const double t = tile_dim(c);
-    const double eff = (double)m * n / (round_up(m, t) * round_up(n, t));
-    if (eff >= 0.75) return c;
-    if (eff > best_eff) {
-      best_eff = eff;
-      best = c;
+// calib/b200.json beside the shared library that holds this code.
+std::string default_calib_path() {
+  Dl_info info;
+  if (!dladdr(reinterpret_cast<void*>(&device_model_init), &info) || !info.dli_fname) return {};
+  std::string so = info.dli_fname;
+  const size_t slash = so.rfind('/');
+  const std::string dir = slash == std::string::npos ? "." : so.substr(0, slash);
+  return dir + "/calib/b200.json";
+}
+
+void load_calibration(DeviceModel* dm) {
+  std::string path;
+  if (const char* e = std::getenv("GGEMM_CALIB_JSON")) path = e;
+  if (path.empty()) path = default_calib_path();
+  if (path.empty()) return;
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) return;
+  static char buf[1 << 16];  // the scalar fields come first in the file
+  const size_t n = std::fread(buf, 1, sizeof buf - 1, f);
+  buf[n] = 0;
+  std::fclose(f);
+  struct Field {
+    const char* key;
+    double* dst;
+    double lo, hi;
+  } fields[] = {{"prep_bw", &dm->prep_bw, 1e10, 1e14},
+                {"prep_block_s", &dm->prep_block_s, 0, 1e-3},
+                {"gemm_ops", &dm->gemm_ops, 1e12, 1e17},
+                {"gemm_tile_s", &dm->gemm_tile_s, 0, 1e-3},
+                {"recon_bw", &dm->recon_bw, 1e10, 1e14},
+                {"recon_block_s", &dm->recon_block_s, 0, 1e-3},
+                {"fp64_flops", &dm->fp64_flops, 1e11, 1e16},
+                {"native_problem_s", &dm->native_problem_s, 0, 1e-2}};
+  int got = 0;
+  for (const Field& fd : fields) {
+    double v;
+    if (json_number(buf, fd.key, &v) && v >= fd.lo && v <= fd.hi) {
+      *fd.dst = v;
+      ++got;
     }
   }
-  return best;
+  dm->from_file = got == (int)(sizeof fields / sizeof fields[0]);
 }
 
-// Three dependent stages (prep, residue GEMM, reconstruct) against native DGEMM.
-void cost(const ggemm_problem_t& p, int nm, int cfg, const DeviceModel& dm, double* t_emu,
-          double* t_nat) {
-  const double m = p.m, n = p.n, k = p.k, kp = kp_of(p.k), t = tile_dim(cfg);
-  const double c_rw = (p.beta != 0.0) ? 2.0 : 1.0;
-  const double np = nm + 1;  // residue planes + abs plane
-  const double prep =
-      (kPrepPasses * (m * k + k * n) * 8 + np * (m + n) * kp + 4.0 * kWsIntsPerRow * (m + n)) /
-      dm.mem_bw;
-  const double slots = (double)dm.num_sms * kSlotsPerSm;
-  const double per_tile = 2.0 * t * t * kp / (dm.int8_ops * kTileEff[cfg] / slots);
-  const double gemm =
-      std::ceil(np * tiles_of(p.m, p.n, cfg) / slots) * per_tile + np * m * n * 4 / dm.mem_bw;
-  const double recon = (np * m * n * 4 + c_rw * m * n * 8) / dm.mem_bw;
-  *t_emu = prep + gemm + recon;
-  const double nat_c = 2.0 * m * n * k / dm.fp64_flops;
-  const double nat_m = (m * k + k * n + c_rw * m * n) * 8 / dm.mem_bw;
-  *t_nat = std::max(nat_c, nat_m);
+inline bool same_shape(const ggemm_problem_t& a, const ggemm_problem_t& b) {
+  return a.m == b.m && a.n == b.n && a.k == b.k && (a.beta != 0.0) == (b.beta != 0.0);
+}
+inline uint32_t shape_hash(const ggemm_problem_t& p) {
+  uint64_t h = (uint64_t)(uint32_t)p.m * 0x9E3779B97F4A7C15ull;
+  h ^= (uint64_t)(uint32_t)p.n * 0xC2B2AE3D27D4EB4Full;
+  h ^= (uint64_t)(uint32_t)p.k * 0x165667B19E3779F9ull;
+  h ^= (p.beta != 0.0) ? 0x27D4EB2F165667C5ull : 0;
+  h ^= h >> 29;
+  h *= 0xBF58476D1CE4E5B9ull;
+  return (uint32_t)(h ^ (h >> 32));
 }
 
-// Wave quantization: shrink the tile of problems whose single tile outweighs a slot's share of
-// the group, until stable.  True if any tile class changed.
-bool tune_tiles(const ggemm_problem_t* probs, int num, const DeviceModel& dm, PlanEntry* out) {
-  const double slots = (double)dm.num_sms * kSlotsPerSm;
-  bool any = false;
-  for (int pass = 0; pass < kTileCfgs; ++pass) {
-    double W = 0;
-    for (int g = 0; g < num; ++g) {
-      if (out[g].route != kRouteEmu) continue;
-      const double t = tile_dim(out[g].tile_cfg);
-      W += (out[g].num_moduli + 1) * tiles_of(probs[g].m, probs[g].n, out[g].tile_cfg) * t * t *
-           kp_of(probs[g].k);
-    }
-    if (W <= 0) return any;
-    const double per_slot = W / slots;
-    bool changed = false;
-    for (int g = 0; g < num; ++g) {
-      if (out[g].route != kRouteEmu || out[g].tile_cfg >= kTileCfgs - 1) continue;
-      const double t = tile_dim(out[g].tile_cfg);
-      if (t * t * kp_of(probs[g].k) > per_slot) {
-        out[g].tile_cfg++;
-        changed = true;
-      }
-    }
-    if (!changed) return any;
-    any = true;
-  }
-  return any;
-}
-
-// Everything after the alpha == 0 check depends only on (m, n, k, beta != 0).
+// Everything after the alpha == 0 check depends only on (m, n, k, beta != 0).  Rule routes and
+// the moduli count as in the reference (src/planner.cpp:286-330); the AUTO cost decision from
+// this library's model.
 int plan_shape(const ggemm_problem_t& p, const ggemm_config_t* cfg, bool autop, int allow_fb,
                double rho_budget, const DeviceModel& dm, PlanEntry& e) {
   if (p.k > kMaxKExact) {
@@ -119,8 +136,9 @@ int plan_shape(const ggemm_problem_t& p, const ggemm_config_t* cfg, bool autop, 
     return GGEMM_OK;
   }
   if (!autop) return GGEMM_OK;
-  e.tile_cfg = tile_by_padding(p.m, p.n);
-  cost(p, e.num_moduli, e.tile_cfg, dm, &e.t_emu_s, &e.t_native_s);
+  const bool bnz = p.beta != 0.0;
+  e.t_emu_s = emu_time(p.m, p.n, p.k, bnz, e.num_moduli, dm);
+  e.t_native_s = native_time(p.m, p.n, p.k, bnz, dm);
   if (allow_fb) {
     if ((double)p.m * p.n * p.k < dm.tiny_mnk) e.route = kRouteTiny;
     else if (e.t_emu_s > e.t_native_s) e.route = kRouteUnprofitable;
@@ -128,47 +146,27 @@ int plan_shape(const ggemm_problem_t& p, const ggemm_config_t* cfg, bool autop, 
   return GGEMM_OK;
 }
 
-inline bool same_shape(const ggemm_problem_t& a, const ggemm_problem_t& b) {
-  return a.m == b.m && a.n == b.n && a.k == b.k && (a.beta != 0.0) == (b.beta != 0.0);
-}
-inline uint32_t shape_hash(const ggemm_problem_t& p) {
-  uint64_t h = (uint64_t)(uint32_t)p.m * 0x9E3779B97F4A7C15ull;
-  h ^= (uint64_t)(uint32_t)p.n * 0xC2B2AE3D27D4EB4Full;
-  h ^= (uint64_t)(uint32_t)p.k * 0x165667B19E3779F9ull;
-  h ^= (p.beta != 0.0) ? 0x27D4EB2F165667C5ull : 0;
-  h ^= h >> 29;
-  h *= 0xBF58476D1CE4E5B9ull;
-  return (uint32_t)(h ^ (h >> 32));
-}
-
-double env_double(const char* name, double lo, double hi, bool* used) {
-  const char* s = std::getenv(name);
-  if (!s || !*s) return 0;
-  char* end = nullptr;
-  const double v = std::strtod(s, &end);
-  if (end == s || !(v >= lo && v <= hi)) {
-    std::fprintf(stderr, "[ggemm] WARNING: %s=%s outside [%g, %g], ignored\n", name, s, lo, hi);
-    return 0;
-  }
-  *used = true;
-  return v;
-}
-
-bool json_number(const char* txt, const char* key, double* v) {
-  char pat[96];
-  std::snprintf(pat, sizeof pat, "\"%s\"", key);
-  const char* p = std::strstr(txt, pat);
-  if (!p) return false;
-  p = std::strchr(p + std::strlen(pat), ':');
-  if (!p) return false;
-  char* end = nullptr;
-  const double x = std::strtod(p + 1, &end);
-  if (end == p + 1 || !(x > 0)) return false;
-  *v = x;
-  return true;
-}
-
 }  // namespace
+
+double emu_time(int m, int n, int k, bool beta_nonzero, int N, const DeviceModel& dm) {
+  const double M = m, Nn = n, kp = (double)(((size_t)k + 31) / 32 * 32), np = N + 1;
+  const double sms = std::max(1, dm.num_sms);
+  const double prep_bytes = 8.0 * (M * k + (double)k * Nn) + np * (M + Nn) * kp + 16.0 * (M + Nn);
+  const double prep_blocks = (double)((m + 31) / 32 + (n + 7) / 8);
+  const double ops = 2.0 * (double)((m + 127) / 128 * 128) * (double)((n + 15) / 16 * 16) * kp * np;
+  const double tiles = np * (double)((m + 127) / 128) * (double)(n > 128 ? (n + 255) / 256 : 1);
+  const double recon_bytes =
+      (N + 4.0) * M * Nn + 8.0 * M * Nn * (beta_nonzero ? 2.0 : 1.0) + 16.0 * (M + Nn);
+  const double recon_blocks = (double)((n + 15) / 16) * (double)((m + 127) / 128);
+  return prep_bytes / dm.prep_bw + prep_blocks * dm.prep_block_s / sms + ops / dm.gemm_ops +
+         tiles * dm.gemm_tile_s / sms + recon_bytes / dm.recon_bw +
+         recon_blocks * dm.recon_block_s / sms;
+}
+
+double native_time(int m, int n, int k, bool beta_nonzero, const DeviceModel& dm) {
+  (void)beta_nonzero;
+  return 2.0 * (double)m * n * k / dm.fp64_flops + dm.native_problem_s;
+}
 
 double env_rho_budget() {
   const char* s = std::getenv("GGEMM_RHO_BUDGET");
@@ -178,49 +176,19 @@ double env_rho_budget() {
   return (end != s && v > 0) ? v : kRhoBudgetDefault;
 }
 
-void device_model_init(DeviceModel* dm, int cc_major, int num_sms) {
-  double fp64, i8, bw;
-  if (cc_major == 10) {
-    // B200: native DGEMM ~36 TF/s, this library's INT8 residue GEMM and HBM3e copy bandwidth
-    // (measured on this pool's B200s: 6.5 TB/s copy).
-    fp64 = 36e12;
-    i8 = 2.5e15;
-    bw = 6.0e12;
-  } else if (cc_major == 9) {
-    fp64 = 67e12 * 0.8;
-    i8 = 1979e12 * 0.5;
-    bw = 3.35e12 * 0.8;
-  } else {
-    fp64 = 10e12;
-    i8 = 200e12;
-    bw = 1e12;
-  }
-  if (const char* path = std::getenv("GGEMM_CALIB_JSON")) {
-    if (FILE* f = std::fopen(path, "rb")) {
-      static char buf[1 << 16];
-      const size_t n = std::fread(buf, 1, sizeof buf - 1, f);
-      buf[n] = 0;
-      std::fclose(f);
-      double v;
-      if (json_number(buf, "f64_peak_flops", &v) && v >= 1e11 && v <= 1e16) fp64 = v;
-      if (json_number(buf, "i8_peak_ops", &v) && v >= 1e12 && v <= 1e17) i8 = v;
-      if (json_number(buf, "bw_Bps", &v) && v >= 1e10 && v <= 1e14) bw = v;
-    }
-  }
+void device_model_init(DeviceModel* dm, int num_sms) {
+  *dm = kB200Default;
+  load_calibration(dm);
   bool used = false;
   double v = env_double("GGEMM_FP64_FLOPS", 1e11, 1e16, &used);
-  if (used) fp64 = v;
+  if (used) dm->fp64_flops = v;
   used = false;
   v = env_double("GGEMM_INT8_OPS", 1e12, 1e17, &used);
-  if (used) i8 = v;
+  if (used) dm->gemm_ops = v;
   used = false;
   v = env_double("GGEMM_MEM_BW", 1e10, 1e14, &used);
-  if (used) bw = v;
+  if (used) dm->prep_bw = dm->recon_bw = v;
   dm->num_sms = num_sms > 0 ? num_sms : 1;
-  dm->fp64_flops = fp64;
-  dm->int8_ops = i8;
-  dm->mem_bw = bw;
-  dm->tiny_mnk = 32.0 * 32.0 * 32.0;
   if (const char* s = std::getenv("GGEMM_TINY_MNK")) {
     char* end = nullptr;
     const double t = std::strtod(s, &end);
@@ -283,14 +251,6 @@ int plan_group(const ggemm_problem_t* probs, int num, const ggemm_config_t* cfg,
     }
     const int r = plan_shape(p, cfg, autop, allow_fb, rho_budget, dm, e);
     if (r) return r;
-  }
-  if (autop && tune_tiles(probs, num, dm, out)) {
-    for (int g = 0; g < num; ++g) {
-      PlanEntry& e = out[g];
-      if (e.route != kRouteEmu) continue;
-      cost(probs[g], e.num_moduli, e.tile_cfg, dm, &e.t_emu_s, &e.t_native_s);
-      if (allow_fb && e.t_emu_s > e.t_native_s) e.route = kRouteUnprofitable;
-    }
   }
   return GGEMM_OK;
 }

@@ -1,10 +1,12 @@
 // planner.hpp -- per-problem routing, moduli count and cost model (host only).
 //
-// Decisions follow the reference planner (src/planner.h:7-83, src/planner.cpp:132-330) so that
-// a call routes every problem the same way: EMPTY / K_ZERO / ALPHA_ZERO / K_TOO_LARGE /
-// SMALL_K / PRECISION by rule, TINY / UNPROFITABLE by a throughput model (AUTO only).  The
-// model's constants come from a device model; for a B200 they are this library's own
-// measurements (see ggemm.cpp), overridable with the same environment variables.
+// Routing rules follow the reference planner (src/planner.h:7-83, src/planner.cpp:286-330) so a
+// call routes every problem the same way where a rule decides: EMPTY / K_ZERO / ALPHA_ZERO /
+// K_TOO_LARGE / SMALL_K / PRECISION / TINY, and the same moduli count.  Where the reference asks
+// its throughput model (AUTO: emulate, or native as UNPROFITABLE), this library asks a model of
+// its own B200 kernels (prep, paired / single-CTA residue GEMM, reconstruct) against cuBLAS
+// DGEMM, whose constants are fitted on the device by calib/calibrate.py and read from
+// calib/b200.json next to the library (or $GGEMM_CALIB_JSON).
 #pragma once
 #include <cstddef>
 
@@ -34,18 +36,32 @@ inline bool route_is_fallback(int r) {
 struct PlanEntry {
   int route;       // Route
   int num_moduli;  // valid for kRouteEmu
-  int tile_cfg;    // cost-model tile class: 0 = 128, 1 = 64, 2 = 32
+  int tile_cfg;    // always 0 (the reference's tile classes do not exist here)
   double t_emu_s, t_native_s;
 };
 
+// Cost model of this library's kernels and of cuBLAS DGEMM on one device (calib/calibrate.py):
+//   prep   bytes / prep_bw   + blocks x prep_block_s / num_sms   (blocks: 32 A rows / 8 B cols)
+//   gemm   ops / gemm_ops    + tiles x gemm_tile_s / num_sms    (ops over 128-row padded tiles)
+//   recon  bytes / recon_bw  + blocks x recon_block_s / num_sms (blocks: 128 rows x 16 cols)
+//   native 2 m n k / fp64_flops + native_problem_s
 struct DeviceModel {
   int num_sms;
-  double fp64_flops, int8_ops, mem_bw, tiny_mnk;
+  double prep_bw, prep_block_s, gemm_ops, gemm_tile_s, recon_bw, recon_block_s;
+  double fp64_flops, native_problem_s;
+  double tiny_mnk;  // AUTO: problems with m n k below it go native (TINY), as in the reference
+  int from_file;    // 1 if the constants came from a calibration file
 };
 
-// B200 model: measured or nominal values, then GGEMM_FP64_FLOPS / GGEMM_INT8_OPS / GGEMM_MEM_BW
-// / GGEMM_TINY_MNK / GGEMM_CALIB_JSON overrides (same names as the reference).
-void device_model_init(DeviceModel* dm, int cc_major, int num_sms);
+// The model for a device with num_sms SMs: the calibration file ($GGEMM_CALIB_JSON, else
+// calib/b200.json next to this library) or built-in B200 values, then the reference's override
+// variables: GGEMM_FP64_FLOPS (fp64_flops), GGEMM_INT8_OPS (gemm_ops), GGEMM_MEM_BW (prep_bw and
+// recon_bw), GGEMM_TINY_MNK.
+void device_model_init(DeviceModel* dm, int num_sms);
+
+// Modelled seconds of one problem emulated with N moduli, and natively.
+double emu_time(int m, int n, int k, bool beta_nonzero, int N, const DeviceModel& dm);
+double native_time(int m, int n, int k, bool beta_nonzero, const DeviceModel& dm);
 
 // Fixed N from cfg, else the normwise choice for (k, target); -1 if unreachable.
 int plan_num_moduli(const ggemm_config_t* cfg, int k);

@@ -34,18 +34,15 @@ int find(std::vector<int>& par, int x) {
   return x;
 }
 
+// Modelled seconds of a problem restricted to `cols` columns: the planner's model of the
+// emulated pipeline (adaptive moduli count), or native DGEMM when no count reaches 1e-15.
 double problem_cost(const ggemm_problem_t& p, const DeviceModel& dm, int cols) {
   if (p.m <= 0 || cols <= 0) return 0.0;
-  const double m = p.m, n = cols, k = p.k;
-  if (p.k <= 0 || p.alpha == 0.0) return 2.0 * m * n * 8 / dm.mem_bw;  // C = beta C
+  if (p.k <= 0 || p.alpha == 0.0) return 2.0 * p.m * cols * 8 / dm.recon_bw;  // C = beta C
   int N = g2::choose_num_moduli(p.k, 1e-15);
-  if (N < 0) return 2.0 * m * n * k / dm.fp64_flops;  // native
+  if (N < 0) return g2::native_time(p.m, cols, p.k, p.beta != 0.0, dm);
   N = std::min(std::max(N, 2), g2::kMaxModuli);
-  const double kp = std::ceil(k / 32.0) * 32.0, np = N + 1;
-  const double prep = (8.0 * (m * k + k * n) + np * (m + n) * kp) / dm.mem_bw;
-  const double gemm = 2.0 * m * n * kp * np / dm.int8_ops;
-  const double recon = (4.0 * np * m * n + 16.0 * m * n) / dm.mem_bw;
-  return prep + std::max(gemm, 4.0 * np * m * n / dm.mem_bw) + recon;
+  return g2::emu_time(p.m, cols, p.k, p.beta != 0.0, N, dm);
 }
 
 }  // namespace
@@ -57,7 +54,7 @@ extern "C" int ggemm_shard_group(const ggemm_problem_t* probs, int num, int S,
     return GGEMM_ERR_INVALID;
   *num_out = 0;
   DeviceModel dm{};
-  g2::device_model_init(&dm, 10, 148);
+  g2::device_model_init(&dm, 148);
   // components of problems linked through a shared A or B operand
   std::vector<int> par(num);
   for (int g = 0; g < num; ++g) par[g] = g;

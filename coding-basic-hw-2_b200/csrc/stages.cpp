@@ -223,7 +223,12 @@ extern "C" int ggemm_stage_plan(const ggemm_problem_t* problems, int num,
                                 int* num_moduli, int* tile_cfg) {
   if (num < 0 || (num > 0 && (!problems || !route || !num_moduli || !tile_cfg)))
     return GGEMM_ERR_INVALID;
-  DeviceModel dm{num_sms, fp64_flops, int8_ops, mem_bw, tiny_mnk};
+  DeviceModel dm{};
+  device_model_init(&dm, num_sms > 0 ? num_sms : 148);  // calibration file, environment
+  if (fp64_flops > 0) dm.fp64_flops = fp64_flops;
+  if (int8_ops > 0) dm.gemm_ops = int8_ops;
+  if (mem_bw > 0) dm.prep_bw = dm.recon_bw = mem_bw;
+  if (tiny_mnk >= 0) dm.tiny_mnk = tiny_mnk;
   std::vector<PlanEntry> out((size_t)std::max(num, 1));
   const int r = plan_group(problems, num, cfg, (ggemm_path_t)path, dm,
                            rho_budget > 0 ? rho_budget : env_rho_budget(), out.data(), nullptr,

@@ -150,8 +150,11 @@ int ggemm_stage_recon(const ggemm_recon_desc_t* descs, int num, int repair_mode,
 int ggemm_stage_wait_probe(void* counters, long long wait_ns, cudaStream_t s);
 
 /* Host-only planner seam (replaces ggemm_plan, src/planner.cpp:281-330): plans num problems
- * for the given path with an explicit device model, writing route / moduli / cost-model tile
- * class per problem (route codes of the reference's ggemm_route_t, src/planner.h:7-17).
+ * for the given path, writing route / moduli / tile class (always 0) per problem (route codes of
+ * the reference's ggemm_route_t, src/planner.h:7-17).  Rule routes and moduli counts are the
+ * reference's; AUTO's cost decision uses this library's calibrated model (calib/b200.json),
+ * whose native DGEMM rate, residue-GEMM rate and stage bandwidth are replaced by fp64_flops,
+ * int8_ops and mem_bw when those are > 0; tiny_mnk >= 0 replaces the TINY threshold.
  * rho_budget <= 0 uses GGEMM_RHO_BUDGET or 16.  Returns GGEMM_OK or GGEMM_ERR_*. */
 int ggemm_stage_plan(const ggemm_problem_t* problems, int num, const ggemm_config_t* cfg,
                      int path, int num_sms, double fp64_flops, double int8_ops, double mem_bw,
