@@ -37,15 +37,21 @@ METRIC = "Effective FP64 TFLOP/s (2Σmnk/t) at 1/2/4/8 B200 vs cuBLAS DGEMM; cer
 REF_SO = os.path.join(ROOT, "oracle", "_ref", "libggemm_ref.so")
 
 
-def make_workload(name: str, world: int, rank: int):
-    """(whole workload, this rank's workload) -- they differ only for weak scaling (C2)."""
+def make_workload(name: str, world: int, rank: int, problems: int = 0):
+    """(whole workload, this rank's workload) -- they differ only for weak scaling (C2).
+    problems > 0 keeps the first `problems` problems (small cases for profiling)."""
     import workloads as W
 
     if name == "c2":
         mine = W.c2(64, W.C2_SEED + rank)
-        return mine, mine
-    wl = W.CONFIGS[name]()
-    return wl, wl
+    else:
+        mine = W.CONFIGS[name]()
+    if problems > 0:
+        mine = W.Workload(mine.name, mine.items[:problems], mine.phi, mine.num_moduli,
+                          mine.path_name, mine.min_k, mine.nonfinite_frac, mine.seed,
+                          mine.scaling, mine.describe + f" (first {problems} problems)",
+                          mine.allow_fallback, mine.target_rel_err)
+    return mine, mine
 
 
 # ------------------------------------------------------------------------------ helpers
@@ -330,12 +336,14 @@ def time_reference_library(g2, wl, grp, cfg, path, stream, steps, torch):
 
 
 def cpu_reference(oracle, shapes, target_s=12.0, threads=0, a_limit=2**26):
-    """Naive FP64 triple loop (the reference's host FP64 path) on host threads over a column
-    sample of the group.  shapes: (m, n, k, alpha, beta, a_id) per problem; problems sharing an
-    a_id share their A matrix.  Problems are taken in order while their A data stays below
-    a_limit elements.  Returns (TFLOP/s, threads, sample description)."""
+    """Naive FP64 triple loop (the reference's host FP64 path) on host threads over a sample of
+    the group: the first `cols` columns of the first `probs` problems, grown from one problem
+    until a run takes at least 0.5 s, then scaled to about target_s.  shapes: (m, n, k, alpha,
+    beta, a_id) per problem; problems sharing an a_id share their A matrix (at most a_limit
+    elements of A are generated).  Returns (TFLOP/s, threads, sample description)."""
     rng = np.random.default_rng(7)
-    a_mats, data, a_elems = {}, [], 0
+    nthreads = threads if threads > 0 else oracle.L.ozo_max_threads()
+    a_mats, a_elems, data = {}, 0, []
     for m, n, k, alpha, beta, aid in shapes:
         if aid not in a_mats:
             if data and a_elems + m * k > a_limit:
@@ -343,30 +351,36 @@ def cpu_reference(oracle, shapes, target_s=12.0, threads=0, a_limit=2**26):
             a_mats[aid] = rng.random(m * k) - 0.5
             a_elems += m * k
         data.append((m, n, k, alpha, beta, a_mats[aid]))
-    nthreads = threads if threads > 0 else oracle.L.ozo_max_threads()
 
-    def run(cols):
+    def run(probs, cols):
         flops = 0.0
-        bufs = []
-        for m, n, k, alpha, beta, A in data:
+        work = []
+        for m, n, k, alpha, beta, A in data[:probs]:
             c = min(n, cols)
-            bufs.append((rng.random(k * c) - 0.5, rng.random(m * c) - 0.5))
+            work.append((m, c, k, alpha, beta, A, rng.random(k * c) - 0.5, rng.random(m * c) - 0.5))
         t0 = time.perf_counter()
-        for (m, n, k, alpha, beta, A), (B, C) in zip(data, bufs):
-            c = min(n, cols)
+        for m, c, k, alpha, beta, A, B, C in work:
             oracle.dgemm_naive(m, c, k, alpha, A, m, B, k, beta, C, m, 0, c, nthreads)
             flops += 2.0 * m * c * k
         return flops, time.perf_counter() - t0
 
-    cols = max(1, nthreads)
-    flops, dt = run(cols)
-    while dt < 0.5 and cols < 4096:
-        cols *= 4
-        flops, dt = run(cols)
-    scale = max(1.0, target_s / max(dt, 1e-6))
-    cols = int(min(4096, cols * scale))
-    flops, dt = run(cols)
-    sample = (f"first {cols} columns of {len(data)} of the {len(shapes)} problems "
+    nmax = max(d[1] for d in data)
+    probs, cols = 1, min(nthreads, nmax)
+    flops, dt = run(probs, cols)
+    while dt < 0.5 and (cols < nmax or probs < len(data)):
+        if cols < nmax:
+            cols = min(nmax, cols * 4)
+        else:
+            probs = min(len(data), probs * 4)
+        flops, dt = run(probs, cols)
+    if dt < 0.5 * target_s:  # scale the sample up towards target_s (a long first run is kept)
+        f = target_s / max(dt, 1e-6)
+        if cols < nmax:
+            cols = int(min(nmax, cols * f))
+        else:
+            probs = int(min(len(data), probs * f))
+        flops, dt = run(probs, cols)
+    sample = (f"first {min(cols, nmax)} columns of the first {probs} of the {len(shapes)} problems "
               f"({flops / 2e9:.1f} GFMA, {dt:.1f} s)")
     return flops / dt / 1e12, nthreads, sample
 
@@ -386,12 +400,12 @@ def run_reference_arm(args):
         return 0
     import g2util
 
-    wl, _ = make_workload(args.workload, world, 0)
+    wl, _ = make_workload(args.workload, world, 0, args.problems)
     oracle = g2util.Oracle()
     shapes = [(it.m, it.n, it.k, it.alpha, it.beta, it.a) for it in wl.items]
     if wl.scaling == "weak":  # the whole job: every rank's group
         for r in range(1, world):
-            w2, _ = make_workload(args.workload, world, r)
+            w2, _ = make_workload(args.workload, world, r, args.problems)
             shapes += [(it.m, it.n, it.k, it.alpha, it.beta, (r, it.a)) for it in w2.items]
     target = max(1.0, 60.0 / max(1, args.steps + args.warmup))
     for _ in range(args.warmup):
@@ -458,7 +472,16 @@ def run_ours(args):
     def total_over_ranks(x):
         return reduce(x, dist.ReduceOp.SUM if world > 1 else None)
 
-    wl_all, wl = make_workload(args.workload, world, rank)
+    phase_t0 = time.perf_counter()
+    phases = {}
+
+    def phase(name):
+        nonlocal phase_t0
+        now = time.perf_counter()
+        phases[name] = round(now - phase_t0, 2)
+        phase_t0 = now
+
+    wl_all, wl = make_workload(args.workload, world, rank, args.problems)
     pieces = (W.shard_pieces(g2, wl, world, rank) if wl.scaling == "strong"
               else W.shard_pieces(g2, wl, 1, 0))
     stream = torch.cuda.Stream(device=dev)
@@ -478,6 +501,8 @@ def run_ours(args):
     os.environ["GGEMM_WORKSPACE_FRACTION"] = str(min(0.55, need / total_mem + 0.002))
     handle = g2.Handle(max(1, grp.num), grp.budget[0] + 1, grp.budget[1] + 1, grp.budget[2] + 1,
                        stream=sptr, min_k=wl.min_k)
+
+    phase("setup")
 
     def call(p=path, probs=None):
         if grp.num == 0:
@@ -525,6 +550,7 @@ def run_ours(args):
     flops_all = total_over_ranks(grp.flops)
     value = flops_all * args.steps / t_max / 1e12
     prep_b, gemm_ops, recon_b = algorithmic(grp, nmods, reuse)
+    phase("device_timing")
     if args.quick:
         line = {"quick": True, "workload": args.workload, "value": value, "unit": "TFLOP/s",
                 "ms_per_step": t_max / args.steps * 1e3, "n_gpus": world,
@@ -602,6 +628,7 @@ def run_ours(args):
     del hA, hB, hC0, hC, bufs, A2, B2, C2
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
+    phase("e2e")
 
     # ------------------------------------------------------- cuBLAS native DGEMM, same data
     for _ in range(2):
@@ -615,6 +642,7 @@ def run_ours(args):
     barrier()
     native_value = flops_all * args.steps / max_over_ranks(
         n_start.elapsed_time(n_stop) / 1e3) / 1e12
+    phase("cublas")
 
     # ------------------------------------------------------------ certified fraction (untimed)
     os.environ["GGEMM_STATS_REPAIR"] = "1"
@@ -634,6 +662,7 @@ def run_ours(args):
                                      + max(0, st2.num_safety_fallback)))
     certified = 100.0 * (1.0 - flagged / max(entries, 1.0))
     torch.cuda.empty_cache()
+    phase("certified")
 
     # ------------------------------------- the reference library built for sm_100a, same data
     refv = None
@@ -646,6 +675,7 @@ def run_ours(args):
         per = max_over_ranks(grp.flops / (v * 1e12) if v else 0.0)
         refv["value"] = (flops_all / per / 1e12) if v and per > 0 else None
     torch.cuda.empty_cache()
+    phase("reference_library")
 
     # ------------------------------------------------------------------------ roofline
     hbm, bf16, peak_kind = measured_peaks()
@@ -653,6 +683,7 @@ def run_ours(args):
         int8_burst, int8 = int8_peak_tops(torch)
     except RuntimeError:
         int8_burst = int8 = None
+    phase("int8_reference")
     stages = {
         "prep_kernel": {"ms": float(stage_ms[0]), "bound": "hbm", "unit": "GB/s",
                         "achieved": prep_b / (stage_ms[0] / 1e3) / 1e9, "peak": hbm,
@@ -691,6 +722,7 @@ def run_ours(args):
         shp = [(it.m, it.n, it.k, it.alpha, it.beta, it.a) for it in wl.items]
         v, cores, sample = cpu_reference(oracle, shp, target_s=args.cpu_seconds)
         cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
+    phase("cpu_baseline")
 
     if rank == 0:
         line = {
@@ -717,6 +749,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "clocks": clk,
             "gpu_launches": launches_per_call * args.steps,
+            "phase_s": phases,
             "peaks": {"hbm_gbs": hbm, "bf16_tflops": bf16, "source": peak_kind,
                       "int8_tops_cublaslt_sustained": int8,
                       "int8_tops_cublaslt_burst": int8_burst},
@@ -740,6 +773,8 @@ def main():
     ap.add_argument("--no-ref-lib", action="store_true",
                     help="skip timing the reference library built for sm_100a")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--problems", type=int, default=0,
+                    help="keep only the first N problems of the workload (profiling cases)")
     ap.add_argument("--quick", action="store_true",
                     help="device-resident timing only (profiling runs): no e2e, cuBLAS, "
                          "certified, reference or CPU legs")
