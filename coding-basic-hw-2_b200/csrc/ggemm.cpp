@@ -461,6 +461,25 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
     if (!loop) jp[jq] = tiles;
     ch.tiles = tiles;
     ch.ragged = gemm_jobs_ragged(jobs, jq);
+    // plane-outer tile numbering when problems of the chunk share an operand and every job has
+    // the same plane count: the prefix then counts one plane's tiles per job
+    ch.plane_outer = false;
+    if (!loop && jq > 1) {
+      bool shared = false, same_planes = true;
+      for (int j = ch.first; j < ch.first + ch.count; ++j)
+        shared = shared || !h->pa_new[j] || !h->pb_new[j];
+      for (int x = 1; x < jq; ++x) same_planes = same_planes && jobs[x].planes == jobs[0].planes;
+      if (shared && same_planes) {
+        ch.plane_outer = true;
+        long long tp = 0;
+        for (int x = 0; x < jq; ++x) {
+          jp[x] = tp;
+          tp += (long long)jobs[x].tm * jobs[x].tn;
+        }
+        jp[jq] = tp;
+        ch.tiles = tp * jobs[0].planes;
+      }
+    }
     for (int x = 0; x < ch.count; ++x) {
       const int j = ch.first + x;
       const int g = emu[j];
@@ -568,14 +587,15 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
       set_gemm_tiling(shape);
       const long long tiles = (long long)shape.tm * shape.tn;
       for (int q = 0; q < planes && tiles > 0; ++q) {
-        if (launch_gemm(jobs + q, jp + 2 * q, 1, tiles, h->counters, s, false))
+        if (launch_gemm(jobs + q, jp + 2 * q, 1, tiles, h->counters, s, 0))
           return GGEMM_ERR_I8GEMM;
         ++*launches;
       }
     } else if (ch.tiles > 0) {
-      const int e =
-          ch.pair ? launch_gemm_pair(jobs, jp, ch.count, ch.tiles, h->counters, s, ch.ragged)
-                  : launch_gemm(jobs, jp, ch.count, ch.tiles, h->counters, s, ch.ragged);
+      const int walk = (ch.ragged ? kGemmWalkBothEnds : 0) |
+                       (ch.plane_outer ? kGemmWalkPlaneOuter : 0);
+      const int e = ch.pair ? launch_gemm_pair(jobs, jp, ch.count, ch.tiles, h->counters, s, walk)
+                            : launch_gemm(jobs, jp, ch.count, ch.tiles, h->counters, s, walk);
       if (e) return GGEMM_ERR_I8GEMM;
       ++*launches;
     }

@@ -53,6 +53,7 @@ struct Chunk {
   bool qscale;  // A images q-scaled (every problem of the chunk in the digit layout)
   bool pair;    // residue GEMM on CTA pairs (launch_gemm_pair)
   bool ragged;  // jobs of different K depth (two-ended tile walk)
+  bool plane_outer;  // tiles numbered plane by plane (problems share operands; kGemmWalkPlaneOuter)
   long long tiles, recon_blocks;
 };
 

@@ -841,26 +841,45 @@ __device__ __forceinline__ TileWalk tile_walk(long long T, int b, int G, bool bo
 // column tiles' B panels in L2 (row tile fastest over a whole plane made them share B but spread
 // over all of A: about ten times the operand bytes read from DRAM, measured).
 constexpr int kBandRows = 2048;
-__device__ __forceinline__ void job_tile(int local, const GemmJob& jb, int& plane, int& tm,
-                                         int& tn) {
+// (tm, tn) of the local tile `local` inside one plane of a job.
+__device__ __forceinline__ void band_tile(int local, const GemmJob& jb, int& tm, int& tn) {
   const int tmc = jb.tm, tnc = jb.tn;
   const int band = max(1, kBandRows / jb.bm);
-  const int per_plane = tmc * tnc;
-  plane = local / per_plane;
-  const int rem = local - plane * per_plane;
-  const int g = rem / (band * tnc);
-  const int within = rem - g * band * tnc;
+  const int g = local / (band * tnc);
+  const int within = local - g * band * tnc;
   const int rows = min(band, tmc - g * band);
   tn = within / rows;
   tm = g * band + (within - tn * rows);
 }
+__device__ __forceinline__ void job_tile(int local, const GemmJob& jb, int& plane, int& tm,
+                                         int& tn) {
+  const int per_plane = jb.tm * jb.tn;
+  plane = local / per_plane;
+  band_tile(local - plane * per_plane, jb, tm, tn);
+}
 
+// Walk flags (kGemmWalk*, host-chosen per launch): alternate both ends of the tile order, and
+// plane-outer numbering.  Plane-outer (groups whose problems share operands, every job with the
+// same plane count): tile t is tile t % T_p of plane t / T_p, with T_p the tiles of one plane
+// over all jobs and prefix[] counting one plane's tiles per job, so that one plane of an operand
+// shared by many problems (a reuse component's A) stays in L2 while those problems stream past
+// it (job-major numbering read the shared A images once per problem: 5x the image bytes from
+// DRAM, measured).
 // Tile t of the call: its job (warp-parallel owner search, so call by all 32 lanes), plane and
 // tile coordinates (a job has fewer than 2^31 tiles).
 __device__ __forceinline__ TileInfo decode_tile(const GemmJob* __restrict__ jobs,
                                                 const long long* __restrict__ prefix, int num,
-                                                long long t) {
+                                                long long t, bool plane_outer) {
   TileInfo ti;
+  if (plane_outer) {
+    const long long tp = prefix[num];
+    ti.plane = (int)(t / tp);
+    const long long r = t - (long long)ti.plane * tp;
+    const int j = find_owner_warp(prefix, num, r);
+    ti.job = jobs + j;
+    band_tile((int)(r - prefix[j]), *ti.job, ti.tm, ti.tn);
+    return ti;
+  }
   const int j = find_owner_warp(prefix, num, t);
   ti.job = jobs + j;
   job_tile((int)(t - prefix[j]), *ti.job, ti.plane, ti.tm, ti.tn);
@@ -871,12 +890,15 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmJob* __restrict__ jobs
 // prefix in `staged` (the still unused operand ring); whole block.
 __device__ __forceinline__ void build_schedule(const GemmJob* __restrict__ jobs,
                                                const long long* __restrict__ prefix, int num,
-                                               const TileWalk& walk, long long* staged,
-                                               int4* sched) {
+                                               const TileWalk& walk, bool plane_outer,
+                                               long long* staged, int4* sched) {
   for (int x = threadIdx.x; x < num; x += blockDim.x) staged[x] = prefix[x];
   __syncthreads();
+  const long long tp = plane_outer ? prefix[num] : 1;
   for (int x = threadIdx.x; x < (int)walk.count(); x += blockDim.x) {
-    const long long t = walk.at(x);
+    long long t = walk.at(x);
+    const int pl = plane_outer ? (int)(t / tp) : 0;
+    if (plane_outer) t -= (long long)pl * tp;
     int lo = 0, hi = num - 1;  // largest j with staged[j] <= t
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
@@ -884,7 +906,12 @@ __device__ __forceinline__ void build_schedule(const GemmJob* __restrict__ jobs,
       else hi = mid - 1;
     }
     int plane, tm, tn;
-    job_tile((int)(t - staged[lo]), jobs[lo], plane, tm, tn);
+    if (plane_outer) {
+      plane = pl;
+      band_tile((int)(t - staged[lo]), jobs[lo], tm, tn);
+    } else {
+      job_tile((int)(t - staged[lo]), jobs[lo], plane, tm, tn);
+    }
     sched[x] = make_int4(lo, plane, tm, tn);
   }
   __syncthreads();  // the staged prefix in the operand ring is no longer read
@@ -1046,7 +1073,7 @@ __device__ __forceinline__ void gemm_tile_epilogue(const GemmJob& jb, const Tile
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const GemmJob* __restrict__ jobs, const long long* __restrict__ prefix, int num,
-                long long total_tiles, DevCounters* cnt, int both_ends) {
+                long long total_tiles, DevCounters* cnt, int walk_flags) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   GemmSmemCtl* ctl = reinterpret_cast<GemmSmemCtl*>(smem + kStages * kStageBytes);
@@ -1073,15 +1100,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  const TileWalk walk = tile_walk(total_tiles, (int)blockIdx.x, (int)gridDim.x, both_ends != 0);
+  const TileWalk walk = tile_walk(total_tiles, (int)blockIdx.x, (int)gridDim.x,
+                                  (walk_flags & kGemmWalkBothEnds) != 0);
+  const bool plane_outer = (walk_flags & kGemmWalkPlaneOuter) != 0;
   int4* sched = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(ctl) +
                                         ((sizeof(GemmSmemCtl) + 63) & ~size_t(63)));
   const bool cached = walk.count() <= kSchedMax && num <= kSchedJobs;  // block-uniform
-  if (cached) build_schedule(jobs, prefix, num, walk, reinterpret_cast<long long*>(smem), sched);
+  if (cached) build_schedule(jobs, prefix, num, walk, plane_outer,
+                              reinterpret_cast<long long*>(smem), sched);
   // tile `it` of this CTA's walk (warp-collective when not cached)
   auto tile_of = [&](long long it) -> TileInfo {
     if (cached) return sched_tile(jobs, sched[it]);
-    return decode_tile(jobs, prefix, num, walk.at(it));
+    return decode_tile(jobs, prefix, num, walk.at(it), plane_outer);
   };
 
   if (warp == 0) {
@@ -1267,7 +1297,7 @@ __device__ __forceinline__ bool bounded_wait_pair(uint64_t* bar, uint32_t parity
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_pair_kernel(const GemmJob* __restrict__ jobs, const long long* __restrict__ prefix,
-                     int num, long long total_tiles, DevCounters* cnt, int both_ends) {
+                     int num, long long total_tiles, DevCounters* cnt, int walk_flags) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   GemmSmemCtl2* ctl = reinterpret_cast<GemmSmemCtl2*>(smem + kStages2 * kStageBytes2);
@@ -1299,14 +1329,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = ctl->tmem_base;
   // the pair's walk: pair b of G pairs (both CTAs of a pair walk the same tiles)
   const TileWalk walk =
-      tile_walk(total_tiles, (int)(blockIdx.x >> 1), (int)(gridDim.x >> 1), both_ends != 0);
+      tile_walk(total_tiles, (int)(blockIdx.x >> 1), (int)(gridDim.x >> 1),
+                (walk_flags & kGemmWalkBothEnds) != 0);
+  const bool plane_outer = (walk_flags & kGemmWalkPlaneOuter) != 0;
   int4* sched = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(ctl) +
                                         ((sizeof(GemmSmemCtl2) + 63) & ~size_t(63)));
   const bool cached = walk.count() <= kSchedMax && num <= kSchedJobs;  // block-uniform
-  if (cached) build_schedule(jobs, prefix, num, walk, reinterpret_cast<long long*>(smem), sched);
+  if (cached) build_schedule(jobs, prefix, num, walk, plane_outer,
+                              reinterpret_cast<long long*>(smem), sched);
   auto tile_of = [&](long long it) -> TileInfo {
     if (cached) return sched_tile(jobs, sched[it]);
-    return decode_tile(jobs, prefix, num, walk.at(it));
+    return decode_tile(jobs, prefix, num, walk.at(it), plane_outer);
   };
   // MMA width of a tile: its columns inside the problem, rounded up to 32 (each CTA then holds
   // a multiple of 16 B rows)
@@ -2020,20 +2053,20 @@ int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, const Pre
 }
 
 int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long long total_tiles,
-                DevCounters* cnt, cudaStream_t s, bool both_ends) {
+                DevCounters* cnt, cudaStream_t s, int walk_flags) {
   if (num <= 0 || total_tiles <= 0) return 0;
   const long long grid = std::min<long long>(total_tiles, (long long)current_device_sms());
   gemm_kernel<<<(unsigned)grid, kGemmThreads, kGemmSmem, s>>>(d_jobs, d_prefix, num, total_tiles,
-                                                              cnt, both_ends ? 1 : 0);
+                                                              cnt, walk_flags);
   return (int)cudaGetLastError();
 }
 
 int launch_gemm_pair(const GemmJob* d_jobs, const long long* d_prefix, int num,
-                     long long total_tiles, DevCounters* cnt, cudaStream_t s, bool both_ends) {
+                     long long total_tiles, DevCounters* cnt, cudaStream_t s, int walk_flags) {
   if (num <= 0 || total_tiles <= 0) return 0;
   const long long pairs = std::min<long long>(total_tiles, (long long)current_device_sms() / 2);
   gemm_pair_kernel<<<(unsigned)(2 * pairs), kGemmThreads, kGemm2Smem, s>>>(
-      d_jobs, d_prefix, num, total_tiles, cnt, both_ends ? 1 : 0);
+      d_jobs, d_prefix, num, total_tiles, cnt, walk_flags);
   return (int)cudaGetLastError();
 }
 

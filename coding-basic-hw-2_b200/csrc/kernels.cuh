@@ -162,10 +162,14 @@ inline void prep_partition(ggemm_prep_desc_t* descs, int num, int* prefix, PrepS
 // One launch per non-empty class; *launches, when given, is increased by their number.
 int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, const PrepSplit& sp,
                 DevCounters* cnt, cudaStream_t s, int* launches = nullptr);
-// both_ends: each CTA alternates between the front (deep K) and back (shallow K) of the tile
-// order, so that shallow tiles' epilogues overlap deep tiles' MMAs; pass gemm_jobs_ragged().
+// walk_flags: kGemmWalkBothEnds -- each CTA alternates between the front (deep K) and back
+// (shallow K) of the tile order, so that shallow tiles' epilogues overlap deep tiles' MMAs
+// (pass it when gemm_jobs_ragged()); kGemmWalkPlaneOuter -- tiles numbered plane by plane over
+// all jobs (every job has the same plane count, d_prefix counts one plane's tiles per job and
+// total_tiles = planes x d_prefix[num]), for groups whose problems share operands.
+constexpr int kGemmWalkBothEnds = 1, kGemmWalkPlaneOuter = 2;
 int launch_gemm(const GemmJob* d_jobs, const long long* d_prefix, int num, long long total_tiles,
-                DevCounters* cnt, cudaStream_t s, bool both_ends);
+                DevCounters* cnt, cudaStream_t s, int walk_flags);
 // Whether jobs differ in K depth (the alternating walk pays only then).
 inline bool gemm_jobs_ragged(const GemmJob* jobs, int num) {
   for (int i = 1; i < num; ++i)
@@ -174,7 +178,7 @@ inline bool gemm_jobs_ragged(const GemmJob* jobs, int num) {
 }
 // The paired GEMM (CTA pairs, tcgen05.mma.cta_group::2) over jobs tiled by set_gemm_tiling_pair.
 int launch_gemm_pair(const GemmJob* d_jobs, const long long* d_prefix, int num,
-                     long long total_tiles, DevCounters* cnt, cudaStream_t s, bool both_ends);
+                     long long total_tiles, DevCounters* cnt, cudaStream_t s, int walk_flags);
 // Reconstruct: compiled per repair mode and per class of moduli counts (N = 14, 15, 16 each, the
 // rest together); descriptors sorted by class, class c owning descriptors [first[c],
 // first[c + 1]) and blocks [block0[c], block0[c + 1]) (blocks per descriptor: recon_job_blocks).

@@ -251,7 +251,7 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
   if (d.job_prefix[1] > 0 &&
       launch_gemm(reinterpret_cast<const GemmJob*>(db + offsetof(NoAllocDescs, job)),
                   reinterpret_cast<const long long*>(db + offsetof(NoAllocDescs, job_prefix)), 1,
-                  d.job_prefix[1], cnt, stream, false))
+                  d.job_prefix[1], cnt, stream, 0))
     return GGEMM_ERR_I8GEMM;
   ReconSplit rsp;  // one descriptor: one reconstruct instance
   for (int c = 0; c <= kReconClasses; ++c) {

@@ -153,9 +153,9 @@ extern "C" int ggemm_stage_gemm(const ggemm_gemm_desc_t* descs, int num, void* s
   const GemmJob* dj = reinterpret_cast<const GemmJob*>(db);
   const long long* dp = reinterpret_cast<const long long*>(db + off_p);
   DevCounters* cnt = static_cast<DevCounters*>(counters);
-  const bool ragged = gemm_jobs_ragged(jobs, num);
-  const int e = pair ? launch_gemm_pair(dj, dp, num, tiles, cnt, s, ragged)
-                     : launch_gemm(dj, dp, num, tiles, cnt, s, ragged);
+  const int walk = gemm_jobs_ragged(jobs, num) ? kGemmWalkBothEnds : 0;
+  const int e = pair ? launch_gemm_pair(dj, dp, num, tiles, cnt, s, walk)
+                     : launch_gemm(dj, dp, num, tiles, cnt, s, walk);
   return e ? GGEMM_ERR_I8GEMM : GGEMM_OK;
 }
 
