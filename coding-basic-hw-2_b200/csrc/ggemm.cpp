@@ -393,9 +393,15 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
         if (ta != tb) return ta > tb;
         return a < b;
       });
-    // the paired GEMM (256 x 256 tiles on CTA pairs) when its row padding costs little
+    // problems of the chunk that share an operand (tiles numbered plane-outer, below)
+    bool shared = false;
+    for (int j = ch.first; j < ch.first + ch.count; ++j)
+      shared = shared || !h->pa_new[j] || !h->pb_new[j];
+    // the paired GEMM (256 x 256 tiles on CTA pairs) for chunks whose problems share operands,
+    // when its row padding costs little (measured: 3.5 % faster on C5's reuse components, 3 %
+    // slower on C3's independent 8192^3 problems, 7 % slower on the ragged C2 group)
     ch.pair = false;
-    if (!loop && !lbat && h->gemm_pair != 0) {
+    if (!loop && !lbat && h->gemm_pair != 0 && (shared || h->gemm_pair == 1)) {
       if (h->gemm_pair == 1) {
         ch.pair = true;
       } else {
@@ -465,9 +471,7 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
     // the same plane count: the prefix then counts one plane's tiles per job
     ch.plane_outer = false;
     if (!loop && jq > 1) {
-      bool shared = false, same_planes = true;
-      for (int j = ch.first; j < ch.first + ch.count; ++j)
-        shared = shared || !h->pa_new[j] || !h->pb_new[j];
+      bool same_planes = true;
       for (int x = 1; x < jq; ++x) same_planes = same_planes && jobs[x].planes == jobs[0].planes;
       if (shared && same_planes) {
         ch.plane_outer = true;

@@ -79,10 +79,10 @@ inline void set_gemm_tiling_pair(GemmJob& j) {
   j.rga = (j.m + 7) / 8;
   j.rgb = (j.n + 7) / 8;
 }
-// Whether a set of problems runs on the paired GEMM: its 256-row tiles pad the rows by at most
-// 2 % more multiply-adds than gemm_kernel's 128-row tiles, and there are tiles for every pair
-// of SMs.  m, n, ksteps, planes per problem.  (Measured: 4 % faster on C5's 4096-row problems,
-// 7 % slower on the ragged C2 group, whose 256-row tiles add 7 % of padding.)
+// Whether a set of problems may run on the paired GEMM: its 256-row tiles pad the rows by at
+// most 2 % more multiply-adds than gemm_kernel's 128-row tiles, and there are tiles for every
+// pair of SMs.  m, n, ksteps, planes per problem.  (The grouped call also asks that the problems
+// share operands; the stage seam asks only this.)
 inline bool gemm_pair_pays(const int* m, const int* n, const int* ksteps, const int* planes,
                            int num, int num_sms) {
   double w1 = 0, w2 = 0;
