@@ -754,7 +754,9 @@ def run_ours(args):
             "clocks": clk,
             "gpu_launches": launches_per_call * args.steps,
             "phase_s": phases,
-            "host_us_per_call": float(np.min(host_s)) * 1e6 if host_s else None,  # least over steps: a later call also waits for the descriptor slot of the call two before
+            # least over steps: a later call also waits for the descriptor slot of the call two
+            # before it to be consumed by the GPU
+            "host_us_per_call": float(np.min(host_s)) * 1e6 if host_s else None,
             "peaks": {"hbm_gbs": hbm, "bf16_tflops": bf16, "source": peak_kind,
                       "int8_tops_cublaslt_sustained": int8,
                       "int8_tops_cublaslt_burst": int8_burst},
