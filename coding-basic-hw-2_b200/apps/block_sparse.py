@@ -57,10 +57,10 @@ class BSR:
             if i != prev:
                 self.row_first.append(b)
                 prev = i
-            ri, cj = self.size[i], self.size[j]
+            ri, cj = int(self.size[i]), int(self.size[j])
             v = (rng.random((cj, ri)) - 0.5) * np.exp(phi * rng.standard_normal((cj, ri)))
             vals.append((v * np.exp(-rij / 2.0)).reshape(-1))
-            self.off.append(o)
+            self.off.append(o)  # Python ints: the offsets become device pointers
             o += ri * cj
         self.row_first.append(len(self.blocks))
         self.A = torch.from_numpy(np.concatenate(vals)).to(device)
