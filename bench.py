@@ -37,9 +37,12 @@ METRIC = "Effective FP64 TFLOP/s (2Σmnk/t) at 1/2/4/8 B200 vs cuBLAS DGEMM; cer
 REF_SO = os.path.join(ROOT, "oracle", "_ref", "libggemm_ref.so")
 
 
-def make_workload(name: str, world: int, rank: int, problems: int = 0):
+def make_workload(name: str, world: int, rank: int, problems: int = 0, path: str = ""):
     """(whole workload, this rank's workload) -- they differ only for weak scaling (C2).
-    problems > 0 keeps the first `problems` problems (small cases for profiling)."""
+    problems > 0 keeps the first `problems` problems (small cases for profiling); a non-empty
+    `path` (a ggemm_path_t name) replaces the configuration's own path."""
+    import dataclasses
+
     import workloads as W
 
     if name == "c2":
@@ -51,6 +54,9 @@ def make_workload(name: str, world: int, rank: int, problems: int = 0):
                           mine.path_name, mine.min_k, mine.nonfinite_frac, mine.seed,
                           mine.scaling, mine.describe + f" (first {problems} problems)",
                           mine.allow_fallback, mine.target_rel_err)
+    if path:
+        mine = dataclasses.replace(mine, path_name=path,
+                                   describe=mine.describe + f" (path {path})")
     return mine, mine
 
 
@@ -400,12 +406,12 @@ def run_reference_arm(args):
         return 0
     import g2util
 
-    wl, _ = make_workload(args.workload, world, 0, args.problems)
+    wl, _ = make_workload(args.workload, world, 0, args.problems, args.path)
     oracle = g2util.Oracle()
     shapes = [(it.m, it.n, it.k, it.alpha, it.beta, it.a) for it in wl.items]
     if wl.scaling == "weak":  # the whole job: every rank's group
         for r in range(1, world):
-            w2, _ = make_workload(args.workload, world, r, args.problems)
+            w2, _ = make_workload(args.workload, world, r, args.problems, args.path)
             shapes += [(it.m, it.n, it.k, it.alpha, it.beta, (r, it.a)) for it in w2.items]
     target = max(1.0, 60.0 / max(1, args.steps + args.warmup))
     for _ in range(args.warmup):
@@ -481,7 +487,7 @@ def run_ours(args):
         phases[name] = round(now - phase_t0, 2)
         phase_t0 = now
 
-    wl_all, wl = make_workload(args.workload, world, rank, args.problems)
+    wl_all, wl = make_workload(args.workload, world, rank, args.problems, args.path)
     pieces = (W.shard_pieces(g2, wl, world, rank) if wl.scaling == "strong"
               else W.shard_pieces(g2, wl, 1, 0))
     stream = torch.cuda.Stream(device=dev)
@@ -782,6 +788,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--problems", type=int, default=0,
                     help="keep only the first N problems of the workload (profiling cases)")
+    ap.add_argument("--path", default="",
+                    choices=["", "native_loop", "native_grouped", "emu_loop", "emu_loop_batched",
+                             "emu_grouped", "auto", "emu_grouped_reuse"],
+                    help="run the workload on this path instead of its configured one")
     ap.add_argument("--quick", action="store_true",
                     help="device-resident timing only (profiling runs): no e2e, cuBLAS, "
                          "certified, reference or CPU legs")
