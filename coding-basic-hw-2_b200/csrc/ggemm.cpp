@@ -607,7 +607,8 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
     if (ch.recon_blocks > 0) {
       if (launch_recon(reinterpret_cast<const ggemm_recon_desc_t*>(db + ch.off_recon),
                        reinterpret_cast<const long long*>(db + ch.off_recon_prefix),
-                       ch.recon_split, repair, h->counters, s, launches))
+                       ch.recon_split, repair, h->counters, s, launches,
+                       /*nonfinite_hint=*/true))
         return GGEMM_ERR_NUMERICS;
     }
     if (!mark(3)) return GGEMM_ERR_CUDA;

@@ -1658,10 +1658,7 @@ __device__ __forceinline__ void recon_entry(const ggemm_recon_desc_t& d, const R
   const int rsh = d.alpha == 0.0 ? 0 : d.rs[i], csh = d.alpha == 0.0 ? 0 : d.cs[j];
   const int sig = d.alpha == 0.0 ? 0 : d.rs[d.m + i], tau = d.alpha == 0.0 ? 0 : d.cs[d.n + j];
   if (const int sp = recon_special(d, cp, c0, rsh, csh, sig, tau)) {
-    if (sp == 2) {
-      dot_entry(d, i, j, cp, c0);
-      ++n_saf;
-    }
+    n_saf += sp == 2 ? 1u : 0u;  // computed by safety_kernel
     return;
   }
   int32_t v[kMaxModuli + 1];
@@ -1720,10 +1717,7 @@ __device__ __forceinline__ void recon_pair(const ggemm_recon_desc_t& d, const Re
     const double c0 = (beta == 0.0) ? 0.0 : *cp;
     const int rsh = x ? rsh2.y : rsh2.x, sig = x ? sig2.y : sig2.x;
     if (const int sp = recon_special(d, cp, c0, rsh, csh, sig, tau)) {
-      if (sp == 2) {
-        dot_entry(d, i0 + x, j, cp, c0);
-        ++n_saf;
-      }
+      n_saf += sp == 2 ? 1u : 0u;  // computed by safety_kernel
       continue;
     }
     int32_t v[kMaxModuli + 1];
@@ -1915,12 +1909,183 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
         need_rep |= 1u << (xb + x);
     }
   }
-  n_saf += __popc(need_saf);
+  n_saf += __popc(need_saf);  // computed by safety_kernel
   n_rep += __popc(need_rep);
-  for (unsigned need = need_saf | need_rep; need; need &= need - 1) {
+  for (unsigned need = need_rep; need; need &= need - 1) {
     const int x = __ffs(need) - 1;
     double* cp = crow + x * d.ldc;
     dot_entry(d, i, j0 + x, cp, d.beta != 0.0 ? *cp : 0.0);
+  }
+}
+
+// ======================================================================= safety fallback
+// Entries in a row of A or a column of B that holds NaN or Inf (prep's non-finite shift) are not
+// emulated: each becomes alpha * dot + beta * C(i, j), dot the sequential FP64 fma chain over
+// q = 0 .. k-1 from 0.0 (the reference's per-entry loop, src/ozaki2_numerics.cu:445-452, 492-497).
+// The reconstruct only counts them; this kernel computes them in tiles of up to 64 x 64 entries,
+// 4 x 4 per thread, the operands staged in shared memory kSafeK K positions at a time.  Every
+// entry's chain is the same sequence of fma operations (same operands, same order, no padding
+// steps) as the per-entry loop, so the values are the same bit for bit, NaN and Inf included.
+// Work items of a problem (alpha != 0): side R, the poisoned rows of a 64-row tile against a
+// 64-column tile, all written; side C, the poisoned columns of a 64-column tile against a 64-row
+// tile, written only in rows that are not poisoned (side R writes the others).
+constexpr int kSafeTile = 64, kSafeK = 32, kSafeThreads = 256;
+constexpr int kSafeLdB = kSafeTile + 2;  // b rows padded (16-byte aligned, fewer store conflicts)
+
+struct SafeSmem {
+  double a[kSafeK][kSafeTile];  // a[q][r] = A(rows[r], k0 + q)
+  double b[kSafeK][kSafeLdB];   // b[q][c] = B(k0 + q, cols[c])
+  int rows[kSafeTile], cols[kSafeTile];
+  unsigned char write_row[kSafeTile];
+  int nr, nc;
+};
+
+__device__ __forceinline__ long long safety_items(const ggemm_recon_desc_t& d) {
+  if (d.N < 1 || d.N > kMaxModuli || d.m <= 0 || d.n <= 0 || d.k <= 0 || d.alpha == 0.0)
+    return 0;
+  return 2LL * ((d.m + kSafeTile - 1) / kSafeTile) * ((d.n + kSafeTile - 1) / kSafeTile);
+}
+
+// Compacts the indices [i0, i0 + 64) ∩ [0, len) of one side into list[]: with `poisoned` the
+// ones whose shift is non-finite, otherwise all of them (write[], when given, marks the clean
+// ones).  Called by one warp; returns the count.
+__device__ __forceinline__ int safety_list(const int32_t* __restrict__ shift, int i0, int len,
+                                           bool poisoned, int* list, unsigned char* write) {
+  const int lane = threadIdx.x & 31;
+  int n = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int i = i0 + 32 * h + lane;
+    const bool in = i < len;
+    const bool bad = in && __ldg(shift + i) == kShiftNonfinite;
+    const bool take = poisoned ? bad : in;
+    const unsigned msk = __ballot_sync(0xFFFFFFFFu, take);
+    if (take) {
+      const int pos = n + __popc(msk & ((1u << lane) - 1u));
+      list[pos] = i;
+      if (write) write[pos] = bad ? 0 : 1;
+    }
+    n += __popc(msk);
+  }
+  return n;
+}
+
+// Work item t of problem d (every thread of the block calls it).
+__device__ void safety_item(const ggemm_recon_desc_t& d, long long t, SafeSmem& sm) {
+  const int RT = (d.m + kSafeTile - 1) / kSafeTile, CT = (d.n + kSafeTile - 1) / kSafeTile;
+  const long long per = (long long)RT * CT;
+  const bool side_c = t >= per;
+  const long long u = side_c ? t - per : t;
+  const int rt = (int)(u / CT), ct = (int)(u - (long long)rt * CT);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (w == 0) {
+    const int n = safety_list(d.rs, rt * kSafeTile, d.m, !side_c, sm.rows,
+                              side_c ? sm.write_row : nullptr);
+    if (!side_c) {
+      sm.write_row[lane] = 1;
+      sm.write_row[lane + 32] = 1;
+    }
+    if (lane == 0) sm.nr = n;
+  } else if (w == 1) {
+    const int n = safety_list(d.cs, ct * kSafeTile, d.n, side_c, sm.cols, nullptr);
+    if (lane == 0) sm.nc = n;
+  }
+  __syncthreads();
+  const int nr = sm.nr, nc = sm.nc;  // block-uniform
+  if (nr > 0 && nc > 0) {
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // columns 4 tx .., rows 4 ty ..
+    const bool live = 4 * ty < nr && 4 * tx < nc;
+    double acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+    for (int k0 = 0; k0 < d.k; k0 += kSafeK) {
+      const int kq = min(kSafeK, d.k - k0);
+      // A: element e -> row slot e % 64, K position e / 64 (a warp reads consecutive rows of one
+      // column); slots past nr repeat the last row (read, never used)
+#pragma unroll
+      for (int x = 0; x < kSafeK * kSafeTile / kSafeThreads; ++x) {
+        const int e = threadIdx.x + kSafeThreads * x;
+        const int r = e & (kSafeTile - 1), q = e / kSafeTile;
+        const int row = sm.rows[min(r, nr - 1)];
+        sm.a[q][r] = q < kq ? __ldg(d.A + row + (long long)(k0 + q) * d.lda) : 0.0;
+      }
+      // B: element e -> K position e % 32, column slot e / 32 (a warp reads 32 consecutive K
+      // positions of one column)
+#pragma unroll
+      for (int x = 0; x < kSafeK * kSafeTile / kSafeThreads; ++x) {
+        const int e = threadIdx.x + kSafeThreads * x;
+        const int q = e & (kSafeK - 1), c = e / kSafeK;
+        const int col = sm.cols[min(c, nc - 1)];
+        sm.b[q][c] = q < kq ? __ldg(d.B + (k0 + q) + (long long)col * d.ldb) : 0.0;
+      }
+      __syncthreads();
+      if (live) {
+#pragma unroll 4
+        for (int q = 0; q < kq; ++q) {  // exactly the chain's steps k0 .. k0 + kq - 1
+          const double2 a01 = *reinterpret_cast<const double2*>(&sm.a[q][4 * ty]);
+          const double2 a23 = *reinterpret_cast<const double2*>(&sm.a[q][4 * ty + 2]);
+          const double2 b01 = *reinterpret_cast<const double2*>(&sm.b[q][4 * tx]);
+          const double2 b23 = *reinterpret_cast<const double2*>(&sm.b[q][4 * tx + 2]);
+          const double av[4] = {a01.x, a01.y, a23.x, a23.y};
+          const double bv[4] = {b01.x, b01.y, b23.x, b23.y};
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
+        }
+      }
+      __syncthreads();
+    }
+    if (live) {
+      const double alpha = d.alpha, beta = d.beta;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = 4 * ty + i;
+        if (r >= nr || !sm.write_row[r]) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = 4 * tx + j;
+          if (c >= nc) continue;
+          double* cp = d.C + sm.rows[r] + (long long)sm.cols[c] * d.ldc;
+          *cp = (beta == 0.0) ? alpha * acc[i][j] : fma(alpha, acc[i][j], beta * *cp);
+        }
+      }
+    }
+  }
+  __syncthreads();  // the next item rebuilds the lists
+}
+
+// The safety blocks of a reconstruct launch (the first G blocks of the first class's grid, so
+// that they run beside the reconstruct blocks): block b of G takes the work items b, b + G, ...
+// of the concatenated numbering (safety_items per descriptor), which every warp derives the same
+// way, 32 descriptors at a time.  hint: prep's count of non-finite rows / columns of this call
+// (0: nothing to do), or nullptr.
+__device__ __noinline__ void safety_blocks(const ggemm_recon_desc_t* __restrict__ descs, int num,
+                                           const unsigned long long* hint, int b, int G) {
+  if (hint && *reinterpret_cast<const volatile unsigned long long*>(hint) == 0) return;
+  __shared__ SafeSmem sm;
+  const int lane = threadIdx.x & 31;
+  long long base = 0, next = b;
+  for (int p0 = 0; p0 < num; p0 += 32) {
+    const int p = p0 + lane;
+    const long long cnt = p < num ? safety_items(descs[p]) : 0;
+    long long incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const long long total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+    while (next < base + total) {
+      // the owner is the first lane whose range ends after `next` (its count is > 0)
+      const int owner = __popc(__ballot_sync(0xFFFFFFFFu, base + incl <= next));
+      const long long start = base + __shfl_sync(0xFFFFFFFFu, incl - cnt, owner);
+      safety_item(descs[p0 + owner], next - start, sm);
+      next += G;
+    }
+    base += total;
   }
 }
 
@@ -1933,8 +2098,13 @@ template <int kMode, int kN>
 __global__ void __launch_bounds__(kReconThreads, 2)
     recon_kernel(const ggemm_recon_desc_t* __restrict__ descs,
                  const long long* __restrict__ prefix, int num, long long block0,
-                 DevCounters* cnt) {
-  const long long bl = block0 + (long long)blockIdx.x;
+                 DevCounters* cnt, const ggemm_recon_desc_t* __restrict__ all_descs, int all_num,
+                 int n_safety, const unsigned long long* hint) {
+  if ((int)blockIdx.x < n_safety) {
+    safety_blocks(all_descs, all_num, hint, (int)blockIdx.x, n_safety);
+    return;
+  }
+  const long long bl = block0 + (long long)blockIdx.x - n_safety;
   const int owner = find_owner_warp(prefix, num, bl);
   const ggemm_recon_desc_t d = descs[owner];
   const long long local = bl - prefix[owner];
@@ -2077,36 +2247,51 @@ int launch_wait_probe(DevCounters* cnt, unsigned long long wait_ns, cudaStream_t
   return (int)cudaGetLastError();
 }
 
+struct SafetyArgs {
+  const ggemm_recon_desc_t* descs;
+  int num, blocks;
+  const unsigned long long* hint;
+};
+
 template <int kMode>
 static void launch_recon_mode(int c, const ggemm_recon_desc_t* dd, const long long* pp, int num,
-                              unsigned grid, long long b0, DevCounters* cnt, cudaStream_t s) {
+                              unsigned grid, long long b0, DevCounters* cnt, const SafetyArgs& sa,
+                              cudaStream_t s) {
+#define G2_RECON(n)                                                                         \
+  recon_kernel<kMode, n><<<grid, kReconThreads, 0, s>>>(dd, pp, num, b0, cnt, sa.descs, sa.num, \
+                                                        sa.blocks, sa.hint)
   switch (c) {
-    case 0: recon_kernel<kMode, 14><<<grid, kReconThreads, 0, s>>>(dd, pp, num, b0, cnt); break;
-    case 1: recon_kernel<kMode, 15><<<grid, kReconThreads, 0, s>>>(dd, pp, num, b0, cnt); break;
-    case 2: recon_kernel<kMode, 16><<<grid, kReconThreads, 0, s>>>(dd, pp, num, b0, cnt); break;
-    default: recon_kernel<kMode, 0><<<grid, kReconThreads, 0, s>>>(dd, pp, num, b0, cnt); break;
+    case 0: G2_RECON(14); break;
+    case 1: G2_RECON(15); break;
+    case 2: G2_RECON(16); break;
+    default: G2_RECON(0); break;
   }
+#undef G2_RECON
 }
 
 int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix,
                  const ReconSplit& sp, int mode, DevCounters* cnt, cudaStream_t s,
-                 int* launches) {
+                 int* launches, bool nonfinite_hint) {
   int n = 0;
+  // the safety blocks ride in the first launch, ahead of its reconstruct blocks
+  SafetyArgs sa{d_descs, sp.first[kReconClasses], 2 * current_device_sms(),
+                nonfinite_hint ? &cnt->nonfinite : nullptr};
   for (int c = 0; c < kReconClasses; ++c) {
     const int f = sp.first[c], num = sp.first[c + 1] - f;
     const long long blocks = sp.block0[c + 1] - sp.block0[c];
     if (num <= 0 || blocks <= 0) continue;
-    if (blocks > 0x7FFFFFFFLL) return (int)cudaErrorInvalidConfiguration;
-    const unsigned grid = (unsigned)blocks;
+    if (blocks + sa.blocks > 0x7FFFFFFFLL) return (int)cudaErrorInvalidConfiguration;
+    const unsigned grid = (unsigned)(blocks + sa.blocks);
     if (mode == GGEMM_STAGE_REPAIR_OFF)
       launch_recon_mode<GGEMM_STAGE_REPAIR_OFF>(c, d_descs + f, d_prefix + f, num, grid,
-                                                sp.block0[c], cnt, s);
+                                                sp.block0[c], cnt, sa, s);
     else if (mode == GGEMM_STAGE_REPAIR_COUNT)
       launch_recon_mode<GGEMM_STAGE_REPAIR_COUNT>(c, d_descs + f, d_prefix + f, num, grid,
-                                                  sp.block0[c], cnt, s);
+                                                  sp.block0[c], cnt, sa, s);
     else
       launch_recon_mode<GGEMM_STAGE_REPAIR_ON>(c, d_descs + f, d_prefix + f, num, grid,
-                                               sp.block0[c], cnt, s);
+                                               sp.block0[c], cnt, sa, s);
+    sa.blocks = 0;
     ++n;
   }
   if (launches) *launches += n;

@@ -215,9 +215,13 @@ inline void recon_partition(ggemm_recon_desc_t* descs, int num, long long* prefi
 // wait_ns and records kStatusProbeTimeout in cnt->status.  It shows the give-up path ends and
 // leaves the context usable, without a fault.  wait_ns is clamped to [1 us, 1 s].
 int launch_wait_probe(DevCounters* cnt, unsigned long long wait_ns, cudaStream_t s);
-// One launch per non-empty class; *launches, when given, is increased by their number.
+// One launch per non-empty class; the first also carries the safety-fallback blocks (entries of
+// NaN / Inf rows and columns, safety_blocks).  *launches, when given, is increased by their
+// number.  nonfinite_hint: cnt->nonfinite holds prep's count of non-finite rows / columns for
+// these descriptors (0 lets the safety blocks return at once); otherwise they scan every tile's
+// shifts.
 int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix,
                  const ReconSplit& sp, int mode, DevCounters* cnt, cudaStream_t s,
-                 int* launches = nullptr);
+                 int* launches = nullptr, bool nonfinite_hint = false);
 
 }  // namespace g2

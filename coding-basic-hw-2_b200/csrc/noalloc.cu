@@ -261,7 +261,7 @@ extern "C" int ggemm_dgemm_noalloc(const ggemm_problem_t* p, int num_moduli, int
   }
   if (launch_recon(reinterpret_cast<const ggemm_recon_desc_t*>(db + offsetof(NoAllocDescs, recon)),
                    reinterpret_cast<const long long*>(db + offsetof(NoAllocDescs, recon_prefix)),
-                   rsp, mode, cnt, stream))
+                   rsp, mode, cnt, stream, nullptr, /*nonfinite_hint=*/true))
     return GGEMM_ERR_NUMERICS;
   return GGEMM_OK;
 }
