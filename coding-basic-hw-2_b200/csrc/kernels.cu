@@ -755,7 +755,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
 }
 
 // ============================================================================== GEMM kernel
-// Tile 128 x 256 (128 x 128 for n <= 128) x (4 x 32-byte K steps) per pipeline stage.
+// Tile 128 x 256 (128 x 128 for n <= 128) x (8 x 32-byte K steps) per pipeline stage.
 // Warp roles:
 //   warp 0: TMEM allocation + bulk-copy producer (lanes [0, kKS) copy A, [kKS, 2 kKS) copy B)
 //   warp 1: tcgen05.mma issuer (one lane)
@@ -767,8 +767,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
 // host-side LPT order; each CTA walks it from both ends when the jobs differ in depth (TileWalk)
 // and keeps its walk's tile
 // coordinates in shared memory (the schedule below).
-constexpr int kKS = 4;     // 32-byte K steps per pipeline stage
-constexpr int kStages = 4;  // kStages * kKS * 12 KB of operands in flight
+// Stages of 8 K steps: a ring of fewer, larger stages measured faster than more, smaller ones of
+// the same bytes (4 x 4 steps: 7.79 ms, 2 x 8: 7.52 ms, one 8192^3 problem at N = 16).
+constexpr int kKS = 8;      // 32-byte K steps per pipeline stage
+constexpr int kStages = 2;  // kStages * kKS * 12 KB of operands in flight
 constexpr int kStepBytesA = 16 * 256;                     // one 32-byte K step of 128 rows
 constexpr int kStepBytesB = 32 * 256;                     // ... of 256 rows
 constexpr int kStageBytes = kKS * (kStepBytesA + kStepBytesB);  // kKS K steps of A and B
@@ -1265,19 +1267,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // Each CTA's producer bulk-copies its own valid row groups into its own shared memory, counted
 // on its own stage barrier (the same data path as gemm_kernel; 2D tensor copies of this layout
 // measured 1.7x slower).  Warp 1 of CTA 1, idle otherwise, relays each of its stages that landed
-// to CTA 0 with one remote arrival on CTA 0's peer_full barrier; CTA 0's MMA thread waits on its
-// own full barrier and on peer_full.  MMA commits multicast to both CTAs' stage-free and
-// accumulator-full barriers; the epilogue warps of both CTAs arrive on CTA 0's accumulator-free
-// barrier.  No load uses cluster multicast.
+// to CTA 0 with one remote arrival on CTA 0's stage barrier, which therefore completes once both
+// CTAs' copies of the stage have landed (two arrivals there, one in CTA 1).  MMA commits
+// multicast to both CTAs' stage-free and accumulator-full barriers; the epilogue warps of both
+// CTAs arrive on CTA 0's accumulator-free barrier.  No load uses cluster multicast.
+// Three stages of 8 K steps (64 KB each): on one C5 reuse component the GEMM took 7.44 ms with
+// six stages of 4 steps, 6.63 ms with four of 6, 6.07-6.29 ms with three of 8 and 6.41 ms with
+// two of 12 (the same 192 KB in every case).
 // Every wait is bounded (kWaitNs).  Copies in flight when a CTA gives up land within
 // microseconds, long before the partner's own bounded waits end and the CTAs pass the final
 // cluster barrier, so neither CTA exits while the other can still touch its shared memory.
-constexpr int kStages2 = 6;
+constexpr int kStages2 = 3;
+constexpr int kKS2 = 8;                                // 32-byte K steps per stage
 constexpr int kStepBytes2 = 16 * 256;                  // one K step of 128 rows
-constexpr int kStageBytes2 = kKS * 2 * kStepBytes2;    // kKS K steps of A and of B
+constexpr int kStageBytes2 = kKS2 * 2 * kStepBytes2;   // kKS2 K steps of A and of B
 constexpr int kGemm2Rows = 256, kGemm2Cols = 256;
 struct GemmSmemCtl2 {
-  uint64_t full[kStages2], peer_full[kStages2], empty[kStages2], acc_full[2], acc_empty[2], drain;
+  uint64_t full[kStages2], empty[kStages2], acc_full[2], acc_empty[2], drain;
   uint32_t tmem_base;
   int abort;
 };
@@ -1306,8 +1312,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages2; ++s) {
-      mbar_init(&ctl->full[s], 1);       // this CTA's producer arms it; its own copies complete it
-      mbar_init(&ctl->peer_full[s], 1);  // (CTA 0) CTA 1's relay, once CTA 1's stage landed
+      // this CTA's producer arms it and its copies complete it; in CTA 0 also CTA 1's relay
+      mbar_init(&ctl->full[s], rank == 0 ? 2 : 1);
       mbar_init(&ctl->empty[s], 1);      // one multicast commit
     }
     for (int b = 0; b < 2; ++b) {
@@ -1367,8 +1373,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const int8_t* B = jb.B + (long long)ti.plane * jb.b_plane + (long long)g0b * 256;
       const long long astep = (long long)jb.rga * 256, bstep = (long long)jb.rgb * 256;
       bool ok = true;
-      for (int ks = 0; ks < jb.ksteps; ks += kKS) {
-        const int nst = min(kKS, jb.ksteps - ks);
+      for (int ks = 0; ks < jb.ksteps; ks += kKS2) {
+        const int nst = min(kKS2, jb.ksteps - ks);
         if (lane == 0) {
           ok = bounded_wait_pair(&ctl->empty[stage], phase ^ 1u, ctl, cnt);
           if (ok) mbar_arrive_expect_tx(&ctl->full[stage], (uint32_t)(nst * (ga + gb) * 256));
@@ -1376,14 +1382,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
         if (!ok) break;
         uint8_t* sa = smem + stage * kStageBytes2;
-        uint8_t* sb = sa + kKS * kStepBytes2;
+        uint8_t* sb = sa + kKS2 * kStepBytes2;
         if (lane < nst) {
           if (ga > 0)
             bulk_g2s(sa + lane * kStepBytes2, A + (long long)(ks + lane) * astep,
                      (uint32_t)(ga * 256), &ctl->full[stage]);
-        } else if (lane >= kKS && lane < kKS + nst) {
+        } else if (lane >= kKS2 && lane < kKS2 + nst) {
           if (gb > 0)
-            bulk_g2s(sb + (lane - kKS) * kStepBytes2, B + (long long)(ks + lane - kKS) * bstep,
+            bulk_g2s(sb + (lane - kKS2) * kStepBytes2, B + (long long)(ks + lane - kKS2) * bstep,
                      (uint32_t)(gb * 256), &ctl->full[stage]);
         }
         __syncwarp();
@@ -1411,16 +1417,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         if (ok) {
           tc_fence_after();
           const uint32_t d_tmem = tmem + (uint32_t)(buf * kGemm2Cols);
-          for (int ks = 0; ks < ksteps; ks += kKS) {
-            const int nst = min(kKS, ksteps - ks);
-            if (!bounded_wait_pair(&ctl->full[stage], phase, ctl, cnt) ||
-                !bounded_wait_pair(&ctl->peer_full[stage], phase, ctl, cnt)) {
+          for (int ks = 0; ks < ksteps; ks += kKS2) {
+            const int nst = min(kKS2, ksteps - ks);
+            if (!bounded_wait_pair(&ctl->full[stage], phase, ctl, cnt)) {
               ok = false;
               break;
             }
             tc_fence_after();
             const uint32_t sa = smem_addr(smem + stage * kStageBytes2);
-            const uint32_t sb = sa + kKS * kStepBytes2;
+            const uint32_t sb = sa + kKS2 * kStepBytes2;
             for (int j = 0; j < nst; ++j) {
               const uint64_t ad = smem_desc_sw32(sa + j * kStepBytes2, 256);
               const uint64_t bd = smem_desc_sw32(sb + j * kStepBytes2, 256);
@@ -1453,12 +1458,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const int ksteps = tile_of(it).job->ksteps;
       bool ok = true;
       if (lane == 0) {
-        for (int ks = 0; ks < ksteps; ks += kKS) {
+        for (int ks = 0; ks < ksteps; ks += kKS2) {
           if (!bounded_wait_pair(&ctl->full[stage], phase, ctl, cnt)) {
             ok = false;
             break;
           }
-          mbar_arrive_cluster(mapa_shared(smem_addr(&ctl->peer_full[stage]), 0));
+          mbar_arrive_cluster(mapa_shared(smem_addr(&ctl->full[stage]), 0));
           if (++stage == kStages2) {
             stage = 0;
             phase ^= 1u;
@@ -2000,27 +2005,41 @@ __device__ void safety_item(const ggemm_recon_desc_t& d, long long t, SafeSmem& 
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
-    for (int k0 = 0; k0 < d.k; k0 += kSafeK) {
+    // the operands of chunk k0 + kSafeK are loaded into registers while chunk k0 is computed
+    constexpr int kPer = kSafeK * kSafeTile / kSafeThreads;
+    double ra[kPer], rb[kPer];
+    auto fetch = [&](int k0) {
       const int kq = min(kSafeK, d.k - k0);
       // A: element e -> row slot e % 64, K position e / 64 (a warp reads consecutive rows of one
       // column); slots past nr repeat the last row (read, never used)
 #pragma unroll
-      for (int x = 0; x < kSafeK * kSafeTile / kSafeThreads; ++x) {
+      for (int x = 0; x < kPer; ++x) {
         const int e = threadIdx.x + kSafeThreads * x;
         const int r = e & (kSafeTile - 1), q = e / kSafeTile;
         const int row = sm.rows[min(r, nr - 1)];
-        sm.a[q][r] = q < kq ? __ldg(d.A + row + (long long)(k0 + q) * d.lda) : 0.0;
+        ra[x] = q < kq ? __ldg(d.A + row + (long long)(k0 + q) * d.lda) : 0.0;
       }
       // B: element e -> K position e % 32, column slot e / 32 (a warp reads 32 consecutive K
       // positions of one column)
 #pragma unroll
-      for (int x = 0; x < kSafeK * kSafeTile / kSafeThreads; ++x) {
+      for (int x = 0; x < kPer; ++x) {
         const int e = threadIdx.x + kSafeThreads * x;
         const int q = e & (kSafeK - 1), c = e / kSafeK;
         const int col = sm.cols[min(c, nc - 1)];
-        sm.b[q][c] = q < kq ? __ldg(d.B + (k0 + q) + (long long)col * d.ldb) : 0.0;
+        rb[x] = q < kq ? __ldg(d.B + (k0 + q) + (long long)col * d.ldb) : 0.0;
+      }
+    };
+    fetch(0);
+    for (int k0 = 0; k0 < d.k; k0 += kSafeK) {
+      const int kq = min(kSafeK, d.k - k0);
+#pragma unroll
+      for (int x = 0; x < kPer; ++x) {
+        const int e = threadIdx.x + kSafeThreads * x;
+        sm.a[e / kSafeTile][e & (kSafeTile - 1)] = ra[x];
+        sm.b[e & (kSafeK - 1)][e / kSafeK] = rb[x];
       }
       __syncthreads();
+      if (k0 + kSafeK < d.k) fetch(k0 + kSafeK);
       if (live) {
 #pragma unroll 4
         for (int q = 0; q < kq; ++q) {  // exactly the chain's steps k0 .. k0 + kq - 1
@@ -2057,17 +2076,26 @@ __device__ void safety_item(const ggemm_recon_desc_t& d, long long t, SafeSmem& 
   __syncthreads();  // the next item rebuilds the lists
 }
 
-// The safety blocks of a reconstruct launch (the first G blocks of the first class's grid, so
-// that they run beside the reconstruct blocks): block b of G takes the work items b, b + G, ...
-// of the concatenated numbering (safety_items per descriptor), which every warp derives the same
-// way, 32 descriptors at a time.  hint: prep's count of non-finite rows / columns of this call
-// (0: nothing to do), or nullptr.
+// The safety blocks of a reconstruct launch (the first blocks of the first class's grid, so that
+// they run beside the reconstruct blocks).  Work items are numbered by concatenating the
+// descriptors' items (safety_items), which every warp derives the same way, 32 descriptors at a
+// time; a block takes the next unclaimed item from *ticket (zeroed before the launch), so the
+// uneven items (K from 1 to many thousands) balance across the blocks.  hint: prep's count of
+// non-finite rows / columns of this call (0: nothing to do), or nullptr.
 __device__ __noinline__ void safety_blocks(const ggemm_recon_desc_t* __restrict__ descs, int num,
-                                           const unsigned long long* hint, int b, int G) {
+                                           const unsigned long long* hint,
+                                           unsigned long long* ticket) {
   if (hint && *reinterpret_cast<const volatile unsigned long long*>(hint) == 0) return;
   __shared__ SafeSmem sm;
+  __shared__ long long s_next;
+  auto claim = [&]() -> long long {
+    __syncthreads();
+    if (threadIdx.x == 0) s_next = (long long)atomicAdd(ticket, 1ull);
+    __syncthreads();
+    return s_next;
+  };
   const int lane = threadIdx.x & 31;
-  long long base = 0, next = b;
+  long long base = 0, next = claim();
   for (int p0 = 0; p0 < num; p0 += 32) {
     const int p = p0 + lane;
     const long long cnt = p < num ? safety_items(descs[p]) : 0;
@@ -2083,7 +2111,7 @@ __device__ __noinline__ void safety_blocks(const ggemm_recon_desc_t* __restrict_
       const int owner = __popc(__ballot_sync(0xFFFFFFFFu, base + incl <= next));
       const long long start = base + __shfl_sync(0xFFFFFFFFu, incl - cnt, owner);
       safety_item(descs[p0 + owner], next - start, sm);
-      next += G;
+      next = claim();
     }
     base += total;
   }
@@ -2101,7 +2129,7 @@ __global__ void __launch_bounds__(kReconThreads, 2)
                  DevCounters* cnt, const ggemm_recon_desc_t* __restrict__ all_descs, int all_num,
                  int n_safety, const unsigned long long* hint) {
   if ((int)blockIdx.x < n_safety) {
-    safety_blocks(all_descs, all_num, hint, (int)blockIdx.x, n_safety);
+    safety_blocks(all_descs, all_num, hint, &cnt->safety_ticket);
     return;
   }
   const long long bl = block0 + (long long)blockIdx.x - n_safety;
@@ -2273,9 +2301,13 @@ int launch_recon(const ggemm_recon_desc_t* d_descs, const long long* d_prefix,
                  const ReconSplit& sp, int mode, DevCounters* cnt, cudaStream_t s,
                  int* launches, bool nonfinite_hint) {
   int n = 0;
-  // the safety blocks ride in the first launch, ahead of its reconstruct blocks
+  // the safety blocks ride in the first launch, ahead of its reconstruct blocks; their work
+  // ticket starts from 0
   SafetyArgs sa{d_descs, sp.first[kReconClasses], 2 * current_device_sms(),
                 nonfinite_hint ? &cnt->nonfinite : nullptr};
+  if (sa.num > 0 &&
+      cudaMemsetAsync(&cnt->safety_ticket, 0, sizeof(cnt->safety_ticket), s) != cudaSuccess)
+    return (int)cudaGetLastError();
   for (int c = 0; c < kReconClasses; ++c) {
     const int f = sp.first[c], num = sp.first[c + 1] - f;
     const long long blocks = sp.block0[c + 1] - sp.block0[c];

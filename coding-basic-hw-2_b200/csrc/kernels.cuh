@@ -17,7 +17,9 @@ struct DevCounters {
   unsigned long long repaired;
   unsigned long long safety;
   unsigned int status;  // 0 = ok; otherwise a kStatus* code set by a kernel
-  unsigned int pad[7];
+  unsigned int pad0;
+  unsigned long long safety_ticket;  // work ticket of the safety-fallback blocks (reconstruct)
+  unsigned int pad[4];
 };
 static_assert(sizeof(DevCounters) == 64, "counter block layout");
 

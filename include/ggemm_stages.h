@@ -126,7 +126,8 @@ typedef struct {
 /* Device scratch a stage call needs for num descriptors (caller-allocated, device memory). */
 size_t ggemm_stage_scratch_bytes(int num);
 /* Device counters: 4 x uint64 {nonfinite vectors, uncertified, repaired, safety fallback}
- * followed by a uint32 status word (0 = ok); 64 bytes, caller-allocated and zeroed. */
+ * followed by a uint32 status word (0 = ok); 64 bytes, caller-allocated and zeroed.  Bytes
+ * 40-47 are scratch of ggemm_stage_recon (a work ticket it zeroes before each launch). */
 #define GGEMM_STAGE_COUNTER_BYTES 64
 
 /* Each enqueues its kernel on `s` (none when there is no work): the GEMM one launch, prep and
