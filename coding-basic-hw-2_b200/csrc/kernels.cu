@@ -220,10 +220,25 @@ __device__ __forceinline__ void load_weights(PrepSmem& sm, int N, int n_cols, bo
 // than it saved (measured), so they start from zero and the epilogue adds the bias.
 constexpr uint32_t kPrepBias = 0x4B400000u;
 
-// Residue byte of t for odd p from tm = kPrepBias + t (low byte of the result; see above).
-__device__ __forceinline__ uint32_t residue_byte(uint32_t tm, float invp, uint32_t p) {
-  const float r = fmaf(__uint_as_float(tm) - 12582912.0f, invp, 12582912.0f);
-  return tm - __float_as_uint(r) * p;
+// Residue bytes of t0, t1 for odd p from tm = kPrepBias + t (low byte of each result; see
+// above): per residue r = fmaf(float(tm) - M, 1/p, M) (the subtraction exact, one rounding to
+// nearest, so bits(r) = bits(M) + rint(t / p)), then tm - bits(r) * p; the two FP32 steps run as
+// packed f32x2 instructions for both residues.
+__device__ __forceinline__ void residue_byte2(uint32_t tm0, uint32_t tm1, float invp, uint32_t p,
+                                              uint32_t& b0, uint32_t& b1) {
+  uint64_t x, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "r"(tm0), "r"(tm1));
+  const uint64_t neg_m = 0xCB400000CB400000ull;  // (-1.5 * 2^23, -1.5 * 2^23)
+  const uint64_t m2 = 0x4B4000004B400000ull;     // (1.5 * 2^23, 1.5 * 2^23)
+  const uint32_t iv = __float_as_uint(invp);
+  uint64_t inv2;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(inv2) : "r"(iv));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(x) : "l"(x), "l"(neg_m));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(inv2), "l"(m2));
+  uint32_t r0, r1;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(r0), "=r"(r1) : "l"(r));
+  b0 = tm0 - r0 * p;
+  b1 = tm1 - r1 * p;
 }
 
 // Sets the n_cols columns of this thread's lane of the accumulator at `acc` to kPrepBias.
@@ -354,10 +369,11 @@ __device__ __forceinline__ void prep_epilogue_n(uint32_t taddr, int8_t* dst, lon
 #pragma unroll
         for (int e = 0; e < 4; ++e) b[e] = v[g & 1][4 * i + e];
       } else {
+        constexpr uint32_t bias = prep_needs_bias(N) ? 0u : kPrepBias;
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          b[e] = residue_byte(v[g & 1][4 * i + e] + (prep_needs_bias(N) ? 0u : kPrepBias),
-                              c_tab.invpf[l], c_tab.p[l]);
+        for (int e = 0; e < 4; e += 2)
+          residue_byte2(v[g & 1][4 * i + e] + bias, v[g & 1][4 * i + e + 1] + bias,
+                        c_tab.invpf[l], c_tab.p[l], b[e], b[e + 1]);
       }
       if (store) *reinterpret_cast<uint32_t*>(dst + l * pb) = pack4(b[0], b[1], b[2], b[3]);
     }
