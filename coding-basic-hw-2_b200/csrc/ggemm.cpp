@@ -397,11 +397,10 @@ int build_emu_call(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* cf
     bool shared = false;
     for (int j = ch.first; j < ch.first + ch.count; ++j)
       shared = shared || !h->pa_new[j] || !h->pb_new[j];
-    // the paired GEMM (256 x 256 tiles on CTA pairs) for chunks whose problems share operands,
-    // when its row padding costs little (measured: 3.5 % faster on C5's reuse components, 3 %
-    // slower on C3's independent 8192^3 problems, 7 % slower on the ragged C2 group)
+    // the paired GEMM (256 x 256 tiles on CTA pairs) when its row padding costs little
+    // (gemm_pair_pays); GGEMM_GEMM_PAIR forces either kernel
     ch.pair = false;
-    if (!loop && !lbat && h->gemm_pair != 0 && (shared || h->gemm_pair == 1)) {
+    if (!loop && !lbat && h->gemm_pair != 0) {
       if (h->gemm_pair == 1) {
         ch.pair = true;
       } else {

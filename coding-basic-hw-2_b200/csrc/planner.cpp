@@ -19,10 +19,10 @@ namespace {
 // found next to the library).
 constexpr DeviceModel kB200Default = {
     148,
-    /*prep_bw=*/2.103e+12, /*prep_block_s=*/2.723e-06,
-    /*gemm_ops=*/2.409e+15, /*gemm_tile_s=*/1.538e-06,
-    /*recon_bw=*/8.432e+12, /*recon_block_s=*/2.883e-06,
-    /*fp64_flops=*/3.132e+13, /*native_problem_s=*/1.041e-07,
+    /*prep_bw=*/2.107e+12, /*prep_block_s=*/2.719e-06,
+    /*gemm_ops=*/2.785e+15, /*gemm_tile_s=*/1.594e-06,
+    /*recon_bw=*/7.89e+12, /*recon_block_s=*/2.822e-06,
+    /*fp64_flops=*/3.138e+13, /*native_problem_s=*/1.068e-07,
     /*tiny_mnk=*/32.0 * 32.0 * 32.0, 0};
 
 bool json_number(const char* txt, const char* key, double* v) {
