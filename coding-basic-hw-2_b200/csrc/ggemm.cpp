@@ -569,6 +569,12 @@ int enqueue_emu_call(ggemm_handle_t h, const EmuCall& c, const ggemm_problem_t* 
   (void)c;
   record = record && h->stage_ev_on && h->chunks.size() == 1;
   auto mark = [&](int i) { return !record || cudaEventRecord(h->stage_ev[i], s) == cudaSuccess; };
+  // prep counts this call's non-finite rows / columns from zero: the reconstruct's safety
+  // blocks read the count to know whether any entry needs them
+  if (!h->chunks.empty() &&
+      cudaMemsetAsync(&h->counters->nonfinite, 0, sizeof(h->counters->nonfinite), s) !=
+          cudaSuccess)
+    return GGEMM_ERR_CUDA;
   for (const Chunk& ch : h->chunks) {
     if (!mark(0)) return GGEMM_ERR_CUDA;
     if (ch.prep_blocks > 0) {

@@ -1679,7 +1679,7 @@ __device__ __forceinline__ void recon_entry(const ggemm_recon_desc_t& d, const R
   const int rsh = d.alpha == 0.0 ? 0 : d.rs[i], csh = d.alpha == 0.0 ? 0 : d.cs[j];
   const int sig = d.alpha == 0.0 ? 0 : d.rs[d.m + i], tau = d.alpha == 0.0 ? 0 : d.cs[d.n + j];
   if (const int sp = recon_special(d, cp, c0, rsh, csh, sig, tau)) {
-    n_saf += sp == 2 ? 1u : 0u;  // computed by safety_kernel
+    n_saf += sp == 2 ? 1u : 0u;  // computed by the safety blocks
     return;
   }
   int32_t v[kMaxModuli + 1];
@@ -1738,7 +1738,7 @@ __device__ __forceinline__ void recon_pair(const ggemm_recon_desc_t& d, const Re
     const double c0 = (beta == 0.0) ? 0.0 : *cp;
     const int rsh = x ? rsh2.y : rsh2.x, sig = x ? sig2.y : sig2.x;
     if (const int sp = recon_special(d, cp, c0, rsh, csh, sig, tau)) {
-      n_saf += sp == 2 ? 1u : 0u;  // computed by safety_kernel
+      n_saf += sp == 2 ? 1u : 0u;  // computed by the safety blocks
       continue;
     }
     int32_t v[kMaxModuli + 1];
@@ -1826,13 +1826,13 @@ __device__ __noinline__ void recon_c32_block(const ggemm_recon_desc_t* __restric
   }
 }
 
-// Reconstruct from the digit layout.  Block: 64 rows x one 32-column record column; thread t
-// takes row 64 b + t / 4 and the 8 columns 8 (t % 4) .. 8 (t % 4) + 7 of the record, so that a
-// warp reads 256 contiguous bytes of each digit plane per load.  The digit and abs-plane loads
-// of a thread (8 bytes per digit plane, 32 bytes of the abs plane) are all issued before its
-// first arithmetic.  The CRT sums run plane by plane over the thread's 8 entries, so each
+// Reconstruct from the digit layout.  Block: kY8Rows rows x one 16-column digit record; thread t
+// takes row kY8Rows b + t / 2 and the 8 columns 8 (t % 2) .. 8 (t % 2) + 7 of the record, so
+// that a warp reads 256 contiguous bytes of each digit plane per load.  The digit and abs-plane
+// loads of a thread (8 bytes per digit plane, 32 bytes of the abs plane) are all issued before
+// its first arithmetic.  The CRT sums run plane by plane over the thread's 8 entries, so each
 // plane's weights are read once per thread instead of once per entry.  Column statistics are
-// staged in shared memory.  Every thread of the block calls it.
+// read per entry (L1 hits).  Every thread of the block calls it.
 template <int kN>
 __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long long local,
                                                int mode, unsigned& n_unc, unsigned& n_rep,
@@ -1930,7 +1930,7 @@ __device__ __forceinline__ void recon_y8_block(const ggemm_recon_desc_t& d, long
         need_rep |= 1u << (xb + x);
     }
   }
-  n_saf += __popc(need_saf);  // computed by safety_kernel
+  n_saf += __popc(need_saf);  // computed by the safety blocks
   n_rep += __popc(need_rep);
   for (unsigned need = need_rep; need; need &= need - 1) {
     const int x = __ffs(need) - 1;
