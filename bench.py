@@ -522,7 +522,9 @@ def run_ours(args):
     for _ in range(args.warmup):
         st = call()
     barrier()
-    launches_per_call = st.kernel_launches
+    # kernel_launches counts the pipeline's kernels (and cuBLAS calls); every call also launches
+    # one kernel that uploads its descriptor blob
+    launches_per_call = st.kernel_launches + 1
     nmod = st.moduli_max
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     for es in ev:

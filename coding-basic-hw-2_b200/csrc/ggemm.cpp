@@ -674,8 +674,7 @@ static int path_native(ggemm_handle_t h, bool grouped, const ggemm_problem_t* pr
     P[cnt + i] = probs[nat[i]].B;
     P[2 * cnt + i] = probs[nat[i]].C;
   }
-  if (cudaMemcpyAsync(h->d_blob[0], hb, 3 * cnt * sizeof(void*), cudaMemcpyHostToDevice,
-                      h->stream) != cudaSuccess)
+  if (launch_blob_upload(h->d_blob[0], h->h_blob_dev[slot], 3 * cnt * sizeof(void*), h->stream))
     return GGEMM_ERR_CUDA;
   r = enqueue_native(h, probs, nat, cnt, true, ng, h->d_blob[0], h->stream,
                      &st->kernel_launches);
@@ -700,9 +699,8 @@ static int path_emu(ggemm_handle_t h, ggemm_path_t path, const ggemm_config_t* c
   st->num_unique_A = c.reuse ? c.num_ua : c.ne;
   st->num_unique_B = c.reuse ? c.num_ub : c.ne;
   st->num_promoted = c.reuse ? c.num_promoted : 0;
-  if (c.blob_bytes)
-    if (cudaMemcpyAsync(db, hb, c.blob_bytes, cudaMemcpyHostToDevice, h->stream) != cudaSuccess)
-      return GGEMM_ERR_CUDA;
+  if (launch_blob_upload(db, h->h_blob_dev[slot], c.blob_bytes, h->stream))
+    return GGEMM_ERR_CUDA;
   r = enqueue_emu_call(h, c, probs, db, repair, path == GGEMM_PATH_EMU_LOOP, true, h->stream,
                        &st->kernel_launches);
   if (!r && c.nn > 0)
@@ -808,7 +806,10 @@ extern "C" int ggemm_create_ex(ggemm_handle_t* out, int max_problems, size_t max
                           3 * sizeof(void*) + 4 * 64;
   h->blob_cap = align_up(P * per_prob + 64 * 1024, kAlign);
   for (int s = 0; s < 2; ++s) {
-    CUA(cudaHostAlloc(&h->h_blob[s], h->blob_cap, cudaHostAllocDefault));
+    CUA(cudaHostAlloc(&h->h_blob[s], h->blob_cap, cudaHostAllocMapped | cudaHostAllocPortable));
+    void* dev_view = nullptr;
+    CUA(cudaHostGetDevicePointer(&dev_view, h->h_blob[s], 0));
+    h->h_blob_dev[s] = dev_view;
     CUA(cudaEventCreateWithFlags(&h->slot_done[s], cudaEventDisableTiming));
     CUA(cudaEventRecord(h->slot_done[s], stream));
   }

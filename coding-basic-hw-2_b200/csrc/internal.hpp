@@ -77,8 +77,10 @@ struct ggemm_handle_s {
   size_t pool_cap = 0;  // bytes
   g2::DevCounters* counters = nullptr;
 
-  // one pinned host descriptor blob per slot, mirrored by one device blob per slot
+  // one pinned, mapped host descriptor blob per slot (h_blob_dev: its device address), copied
+  // into the device blob by launch_blob_upload
   char* h_blob[2] = {nullptr, nullptr};
+  const void* h_blob_dev[2] = {nullptr, nullptr};
   char* d_blob[2] = {nullptr, nullptr};
   size_t blob_cap = 0;
   cudaEvent_t slot_done[2] = {nullptr, nullptr};

@@ -12,6 +12,7 @@
 // src/ozaki2_numerics.cu:8-76 and :112-586; the work decomposition is this library's own.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -2161,6 +2162,23 @@ __global__ void __launch_bounds__(kReconThreads, 2)
   flush_counters(n_unc, n_rep, n_saf, cnt);
 }
 
+// ============================================================ descriptor upload
+// Copies the per-call descriptor blob from pinned, mapped host memory into device memory with the
+// SMs instead of a copy engine.  A cudaMemcpyAsync of the blob queues on the copy engine behind
+// whatever host -> device copies other streams have queued there: in a pipelined caller that copies
+// the next step's inputs (tens of GB) while this step computes, the call's kernels would wait for
+// that whole copy before they could start.  16-byte words, then the tail bytes.
+__global__ void __launch_bounds__(256) blob_upload_kernel(uint4* __restrict__ dst,
+                                                          const uint4* __restrict__ src,
+                                                          long long n16, int tail) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride)
+    dst[i] = src[i];
+  if (blockIdx.x == 0 && threadIdx.x < tail)
+    reinterpret_cast<uint8_t*>(dst + n16)[threadIdx.x] =
+        reinterpret_cast<const uint8_t*>(src + n16)[threadIdx.x];
+}
+
 // ===================================================================================== host
 namespace {
 std::mutex g_dev_mu;
@@ -2240,6 +2258,18 @@ int current_device_sms() {
   if (dev < 0 || dev >= 64) return 148;
   std::lock_guard<std::mutex> lk(g_dev_mu);
   return g_sms[dev] > 0 ? g_sms[dev] : 148;
+}
+
+int launch_blob_upload(void* d_dst, const void* src_dev, size_t bytes, cudaStream_t s) {
+  if (bytes == 0) return 0;
+  if ((((uintptr_t)d_dst | (uintptr_t)src_dev) & 15) != 0) return (int)cudaErrorInvalidValue;
+  const long long n16 = (long long)(bytes / 16);
+  const int tail = (int)(bytes % 16);
+  const long long want = (n16 + 255) / 256;
+  const unsigned grid = (unsigned)std::max(1LL, std::min(want, 4LL * current_device_sms()));
+  blob_upload_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<uint4*>(d_dst),
+                                          reinterpret_cast<const uint4*>(src_dev), n16, tail);
+  return (int)cudaGetLastError();
 }
 
 int launch_prep(const ggemm_prep_desc_t* d_descs, const int* d_prefix, const PrepSplit& sp,

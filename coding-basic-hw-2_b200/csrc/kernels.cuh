@@ -127,6 +127,10 @@ int upload_tables_current_device();
 // Streaming multiprocessors of the current device (cached).
 int current_device_sms();
 
+// Copies `bytes` from pinned, mapped host memory (src_dev: its device address) to device memory
+// d_dst with a kernel (no copy engine, so it does not wait behind other streams' host -> device
+// copies).  Both addresses 16-byte aligned.  Returns a cudaError_t.
+int launch_blob_upload(void* d_dst, const void* src_dev, size_t bytes, cudaStream_t s);
 // Launchers, on `s`: the GEMM one kernel, prep and the reconstruct one kernel per class of
 // moduli counts present.  prefix: device array of num+1 exclusive block / tile prefix sums.
 // Return the cudaError_t of the launches.
