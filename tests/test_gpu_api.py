@@ -112,6 +112,9 @@ WORKLOADS = {
     "ragged": [(7, 13, 33), (100, 70, 50), (33, 65, 200), (128, 96, 300), (1, 300, 64),
                (300, 1, 129), (40, 24, 72), (65, 3, 31)],
     "longk": [(16, 16, 2048), (32, 8, 4096)],
+    # an odd number of problems: NATIVE_GROUPED's pointer table (3 x 8 bytes per problem) is then
+    # not a multiple of 16 bytes, so the descriptor upload kernel copies a tail
+    "odd3": [(48, 40, 96), (17, 33, 5), (64, 80, 128)],
 }
 PATHS = [0, 1, 2, 3, 4, 5, 6]
 
